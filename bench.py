@@ -1,0 +1,464 @@
+#!/usr/bin/env python
+"""Varlen attention fwd+bwd throughput of scree_b200 on B200 (one JSON line).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl native|reference]
+
+Workload (default): cfg4 — 64 sequences, lengths lognormal(ln 2048, 0.6) clipped
+to [16, 16384] at seed 0 (T = 158,330 tokens), q/k/v/dO ~ N(0,1) bf16 of shape
+(T, 32 heads, 128), causal.  A step is one forward + backward through the
+drop-in autograd entry point (varlen_attention_triton_autograd -> out.backward).
+Every q/k/v/dO tensor is 1.3 GB, far larger than the 126 MB L2, so no flush is
+needed between steps.
+
+Multi-GPU (torchrun, one process per GPU): the fixed batch is split by whole
+sequences, longest-processing-time-first on L^2, identically on every rank (the
+plan is broadcast from rank 0 over NCCL as a consistency check).  There is no
+collective on the data path; the step time is the max over ranks (CUDA events,
+all_reduce MAX) and ``value`` = all tokens / that time ("strong" scaling: total
+work fixed).
+
+--impl reference times the reference algorithm on the host CPU instead: the
+numpy oracle (a restatement of scree.kernels.reference; the reference itself is
+pure Python and is not installed on the GPU box), fp32, all host cores, on a
+bounded sample of cfg4's sequences, extrapolated to the whole workload by
+algorithmic FLOPs.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "varlen-attn fwd+bwd tokens/s & TFLOP/s vs TC peak at 1/2/4/8 B200"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+_REASONS = {
+    0x1: "gpu_idle",
+    0x2: "applications_clocks_setting",
+    0x4: "sw_power_cap",
+    0x8: "hw_slowdown",
+    0x10: "sync_boost",
+    0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons every 200 ms through NVML (read only)."""
+
+    def __init__(self, device_index: int):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            handle = None
+            try:
+                import torch
+
+                props = torch.cuda.get_device_properties(device_index)
+                bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+                handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._h = handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.ok = False
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                self.samples.append((mhz, rs))
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def start(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+
+    def stop(self):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= int(r)
+        reasons = [name for b, name in _REASONS.items() if bits & b and name != "gpu_idle"]
+        return {
+            "sm_mhz": float(statistics.median(mhz)),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": reasons,
+            "samples": len(mhz),
+        }
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_reference_rate(lengths, H, D, causal, budget_s=12.0, repeats=2, log=None):
+    """Time the oracle (numpy fp32, all host cores) forward+backward on a bounded
+    sample of the workload's sequences and extrapolate to the whole workload by
+    algorithmic FLOPs.  Returns (tokens/s, cores, sample description)."""
+    import oracle
+    from scree_b200 import workloads
+
+    cores = len(os.sched_getaffinity(0))
+    T_total = sum(lengths)
+    F_total = workloads.attn_flops(lengths, H, D, causal)
+    # Sample: the median-length sequence, all heads (cost per token of the batch
+    # is dominated by pair count, which the FLOP scaling accounts for).
+    order = np.argsort(lengths)
+    L = int(lengths[int(order[len(order) // 2])])
+    rng = np.random.default_rng(0)
+    q, k, v, do = (rng.standard_normal((L, H, D)).astype(np.float32) for _ in range(4))
+    offs = [0, L]
+
+    def run():
+        oracle.attention_fwd(q, k, v, offs, causal=causal, dtype=np.float32)
+        oracle.attention_bwd(do, q, k, v, offs, causal=causal, dtype=np.float32)
+
+    run()  # warm-up
+    times = []
+    t_start = time.perf_counter()
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    t = statistics.median(times)
+    F_sample = workloads.attn_flops([L], H, D, causal)
+    rate = T_total / (t * F_total / F_sample)
+    sample = (f"one sequence of L={L} (cfg4 median) x {H} heads x D={D}, fp32 numpy oracle "
+              f"fwd+bwd, median of {len(times)} after 1 warm-up = {t:.3f} s; extrapolated to "
+              f"all {len(lengths)} sequences by algorithmic FLOPs ({F_total / F_sample:.1f}x)")
+    return rate, cores, sample
+
+
+def run_reference_arm(args, lengths, H, D, causal):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import oracle
+    from scree_b200 import workloads
+
+    cores = len(os.sched_getaffinity(0))
+    order = np.argsort(lengths)
+    L = int(lengths[int(order[len(order) // 2])])
+    rng = np.random.default_rng(0)
+    q, k, v, do = (rng.standard_normal((L, H, D)).astype(np.float32) for _ in range(4))
+    offs = [0, L]
+
+    def step():
+        oracle.attention_fwd(q, k, v, offs, causal=causal, dtype=np.float32)
+        oracle.attention_bwd(do, q, k, v, offs, causal=causal, dtype=np.float32)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    T_total = sum(lengths)
+    F_total = workloads.attn_flops(lengths, H, D, causal)
+    F_sample = workloads.attn_flops([L], H, D, causal)
+    step_full = dt * F_total / F_sample
+    value = T_total / step_full
+    sample = (f"each step: one sequence of L={L} (cfg4 median) x {H} heads x D={D}, numpy oracle "
+              f"(restatement of scree.kernels.reference) fp32 fwd+bwd on {cores} host threads, "
+              f"extrapolated to the whole workload by algorithmic FLOPs ({F_total / F_sample:.1f}x)")
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_full * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": workload_config(args, lengths, H, D, causal, world),
+        "tflops": F_total / step_full / 1e12,
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args, lengths, H, D, causal, world):
+    return {
+        "workload": f"{args.config}: {len(lengths)} seqs lognormal(ln 2048, 0.6) clip [16,16384] seed 0, "
+        f"T={sum(lengths)}, H={H}, D={D}, bf16, {'causal' if causal else 'non-causal'} fwd+bwd",
+        "global_batch": int(sum(lengths)),
+        "seqs": len(lengths),
+        "max_seqlen": int(max(lengths)),
+        "heads": H,
+        "head_dim": D,
+        "causal": causal,
+        "parallelism": f"seq-shard{world}" if world > 1 else "single",
+        "l2": "inputs larger than L2 (each of q/k/v/dO 1.3 GB)",
+    }
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--config", default="cfg4", choices=["cfg4", "cfg2", "cfg5"])
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+
+    from scree_b200 import workloads
+
+    cfg = workloads.attn_config(args.config)
+    lengths = list(cfg.lengths)
+    H, D, causal = cfg.heads, cfg.head_dim, cfg.causal
+
+    if args.impl == "reference":
+        run_reference_arm(args, lengths, H, D, causal)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    from scree_b200 import _lib
+    from scree_b200.kernels.native import varlen_attention_triton_autograd
+
+    # Shard plan: LPT on L^2 (attention cost), broadcast from rank 0.
+    plan = workloads.lpt_partition([L * L for L in lengths], world)
+    if world > 1:
+        obj = [plan]
+        dist.broadcast_object_list(obj, src=0)
+        assert obj[0] == plan, "shard plan differs across ranks"
+    mine = [lengths[i] for i in plan[rank]]
+    T = sum(mine)
+    dt = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(1234 + 17 * rank)
+
+    def rnd():
+        return torch.randn((T, H, D), device=dev, dtype=torch.float32, generator=g).to(dt)
+
+    q, k, v, do = rnd(), rnd(), rnd(), rnd()
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(mine)]), dtype=torch.int32, device=dev)
+
+    def step():
+        for t in (q, k, v):
+            t.grad = None
+        out = varlen_attention_triton_autograd(q, k, v, cu, causal=causal)
+        out.backward(do)
+        return out
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    _lib.profile_read(_lib.PROF_ATTN_FWD)
+    _lib.profile_read(_lib.PROF_ATTN_BWD)
+    _lib.profile_enable(True)
+    n0 = _lib.launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - n0
+    _lib.profile_enable(False)
+    elapsed_ms = ev0.elapsed_time(ev1)
+    fwd_ms, nf = _lib.profile_read(_lib.PROF_ATTN_FWD)
+    bwd_ms, nb = _lib.profile_read(_lib.PROF_ATTN_BWD)
+    if world > 1:
+        dist.barrier()
+    sampler.stop()
+    assert _lib.device_status() == 0, "kernel reported an error (device status word)"
+
+    flops_mine = workloads.attn_flops(mine, H, D, causal)
+    flops_fwd_mine = workloads.attn_flops(mine, H, D, causal, fwd=True, bwd=False)
+    flops_bwd_mine = workloads.attn_flops(mine, H, D, causal, fwd=False, bwd=True)
+    stats = torch.tensor([elapsed_ms, float(T), flops_mine, float(launches)], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = stats.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        max_ms, total_T, total_flops, total_launch = float(mx[0]), float(sm[1]), float(sm[2]), float(sm[3])
+    else:
+        max_ms, total_T, total_flops, total_launch = elapsed_ms, float(T), flops_mine, float(launches)
+    ms_step = max_ms / args.steps
+    value = total_T / (ms_step / 1e3)
+    tflops = total_flops / (ms_step / 1e3) / 1e12
+
+    peaks, peak_kind = load_peaks()
+    peak_tf = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    bwd_avg_ms = bwd_ms / max(nb, 1)
+    fwd_avg_ms = fwd_ms / max(nf, 1)
+    ach_bwd = flops_bwd_mine / (bwd_avg_ms / 1e3) / 1e12
+    ach_fwd = flops_fwd_mine / (fwd_avg_ms / 1e3) / 1e12
+    traffic = None
+    tp = ROOT / "profiles" / "attn_bwd_cfg4_traffic.json"
+    if tp.exists():
+        try:
+            traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+        except Exception:
+            traffic = None
+
+    # ------------------------------------------------------------ end to end
+    e2e = None
+    if not args.no_e2e:
+        hq, hk, hv, hdo = (t.detach().cpu().pin_memory() for t in (q, k, v, do))
+        ho = torch.empty_like(hq).pin_memory()
+        hdq, hdk, hdv = (torch.empty_like(hq).pin_memory() for _ in range(3))
+        dq_ = torch.empty_like(q.detach())
+
+        def e2e_step():
+            dq_in = hq.to(dev, non_blocking=True).requires_grad_(True)
+            dk_in = hk.to(dev, non_blocking=True).requires_grad_(True)
+            dv_in = hv.to(dev, non_blocking=True).requires_grad_(True)
+            ddo = hdo.to(dev, non_blocking=True)
+            out = varlen_attention_triton_autograd(dq_in, dk_in, dv_in, cu, causal=causal)
+            out.backward(ddo)
+            ho.copy_(out.detach(), non_blocking=True)
+            hdq.copy_(dq_in.grad, non_blocking=True)
+            hdk.copy_(dk_in.grad, non_blocking=True)
+            hdv.copy_(dv_in.grad, non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.e2e_steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
+        e_step = float(e_ms[0]) / args.e2e_steps
+        nbytes = q.numel() * q.element_size()
+        e2e = {
+            "value": total_T / (e_step / 1e3),
+            "unit": "tokens/s",
+            "ms_per_step": e_step,
+            "h2d_bytes_per_step": int(4 * nbytes * world),
+            "d2h_bytes_per_step": int(4 * nbytes * world),
+            "path": "varlen_attention_triton_autograd with pinned host q/k/v/dO in, out/dq/dk/dv back to pinned host",
+        }
+        del dq_
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, cores, sample = cpu_reference_rate(lengths, H, D, causal)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": max(3, args.warmup),
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": workload_config(args, lengths, H, D, causal, world),
+            "tflops": tflops,
+            "tflops_frac_of_peak": tflops / peak_tf,
+            "roofline": {
+                "kernel": "attn_bwd_kernel<128, bf16, causal> (dK/dV/dQ, 10*H*D*pairs FLOPs)",
+                "bound": "tensor",
+                "achieved": ach_bwd,
+                "peak": peak_tf,
+                "unit": "TFLOP/s",
+                "frac": ach_bwd / peak_tf,
+                "peak_source": f"{peak_kind} bf16_tflops_sustained (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 1.4 PFLOP/s sustained",
+                "traffic": traffic,
+                "avg_launch_ms": bwd_avg_ms,
+            },
+            "kernels": {
+                "attn_fwd": {"avg_ms": fwd_avg_ms, "launches": nf, "tflops": ach_fwd, "frac": ach_fwd / peak_tf},
+                "attn_bwd": {"avg_ms": bwd_avg_ms, "launches": nb, "tflops": ach_bwd, "frac": ach_bwd / peak_tf},
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(total_launch),
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/*
+ * scree_b200.h — C ABI of libscree_b200.so, the B200 (sm_100a) implementation of
+ * scree's varlen hot path.
+ *
+ * Conventions
+ *  - Every function returns a scree_status; on failure scree_last_error() gives a
+ *    message (thread-local).  Nothing here allocates device memory: callers pass
+ *    outputs and, where a kernel needs scratch, a workspace whose size the
+ *    matching *_workspace_size() function reports.
+ *  - Pointers are device pointers unless the name says host.  `stream` is a
+ *    cudaStream_t (pass 0 for the legacy default stream).  All work is enqueued
+ *    asynchronously on that stream; no function synchronises.
+ *  - Packed ("varlen") tensors follow scree.Array: `values` of shape (T, ...)
+ *    with sequence b occupying rows [offsets[b], offsets[b+1]).  `offsets` is a
+ *    device array of B+1 int32 (offs_is_i64 = 0) or int64 (offs_is_i64 = 1).
+ *  - Row strides are in ELEMENTS.  The innermost (feature / head_dim) stride is 1.
+ */
+#ifndef SCREE_B200_H_
+#define SCREE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SCREE_ABI_VERSION 1
+
+typedef enum {
+  SCREE_OK = 0,
+  SCREE_ERR_INVALID = 1,     /* bad argument: maps to AssertionError / ValueError */
+  SCREE_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. head_dim 96)   */
+  SCREE_ERR_CUDA = 3         /* a CUDA runtime call failed                       */
+} scree_status;
+
+typedef enum { SCREE_F16 = 0, SCREE_BF16 = 1, SCREE_F32 = 2 } scree_dtype;
+
+/* Copies the calling thread's last error message into buf (NUL-terminated). */
+int scree_last_error(char* buf, size_t n);
+/* Returns SCREE_ABI_VERSION. */
+int scree_version(void);
+/* Reads (and optionally clears) the device status word that kernels set when a
+ * bounded wait gave up or an input was out of range.  0 = no error.  This call
+ * synchronises with the device. */
+int scree_device_status(int* status_out, int reset);
+/* Number of kernels this library has launched in the process so far. */
+long long scree_launch_count(void);
+/* Per-kernel timing for benchmarks: when enabled, each main kernel launch is
+ * bracketed by CUDA events on its stream.  scree_profile_read() waits for the
+ * recorded events, returns the summed milliseconds and launch count of one
+ * kernel kind (0 attention fwd, 1 attention bwd, 2 norm fwd, 3 norm bwd) and
+ * clears them.  Neither call has a reference counterpart. */
+int scree_profile_enable(int on);
+int scree_profile_read(int kernel, double* total_ms, long long* launches);
+
+/* ------------------------------------------------------------------ attention
+ * Varlen self-attention forward.
+ * Replaces: scree/kernels/triton/varlen_attention.py:165-268
+ *   varlen_attention_triton(q, k, v, cu_seqlens, causal, block_m, block_n,
+ *                           return_lse, out, lse_buffer)
+ * and the kernel it launches (varlen_attention.py:36-162).
+ * q, k, v, o: (T, H, D) fp16/bf16 with strides (row_stride, head_stride, 1)
+ * in elements; o may alias nothing else.  lse: (T, H) fp32 contiguous, natural
+ * log of the softmax denominator (m + ln l), or NULL.  scale is the softmax
+ * scale (scree uses 1/sqrt(D)).  max_seqlen <= 0 means "unknown": the kernel
+ * then sizes its grid for the worst case (T tokens in one sequence).
+ * D must be 32, 64 or 128.  workspace: scree_attn_fwd_workspace_size() bytes. */
+size_t scree_attn_fwd_workspace_size(int64_t B, int64_t T, int64_t H, int D);
+int scree_attn_fwd(const void* q, const void* k, const void* v, int64_t q_row_stride,
+                   int64_t q_head_stride, int64_t k_row_stride, int64_t k_head_stride,
+                   int64_t v_row_stride, int64_t v_head_stride, const void* offsets,
+                   int offs_is_i64, int64_t B, int64_t T, int64_t H, int D, int dtype,
+                   int causal, float scale, int64_t max_seqlen, void* o, int64_t o_row_stride,
+                   int64_t o_head_stride, float* lse, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* Varlen self-attention backward: dq, dk, dv from do, q, k, v, o, lse.
+ * Replaces: scree/kernels/triton/_backward.py:288-396
+ *   varlen_attention_triton_backward(do, q, k, v, o, lse, cu_seqlens, causal,
+ *                                    block_m, block_n) -> (dq, dk, dv)
+ * and its three kernels (_backward.py:37-69, :73-187, :191-285).
+ * All (T, H, D) tensors here must be contiguous (row stride H*D, head stride D).
+ * lse: (T, H) fp32 from scree_attn_fwd.  workspace: see the size function
+ * (fp32 dQ accumulator + per-row Delta + the tile schedule). */
+size_t scree_attn_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int D);
+int scree_attn_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o,
+                   const float* lse, const void* offsets, int offs_is_i64, int64_t B, int64_t T,
+                   int64_t H, int D, int dtype, int causal, float scale, int64_t max_seqlen,
+                   void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* ------------------------------------------------------------------ norms
+ * RMSNorm forward over the last dim of a (rows, C) row-major buffer.
+ * Replaces: scree/kernels/triton/varlen_rmsnorm.py:49-99 varlen_rmsnorm_triton
+ * (kernel :17-46); numerics follow scree/kernels/reference/varlen_rmsnorm.py:58-65
+ * (fp32 math, weight applied in its own precision).
+ * x, y: dtype; weight: w_dtype or NULL; rstd: (rows,) fp32 or NULL (saved for
+ * the backward).  x_row_stride / y_row_stride in elements. */
+int scree_rmsnorm_fwd(const void* x, int64_t x_row_stride, const void* weight, int w_dtype,
+                      void* y, int64_t y_row_stride, float* rstd, int64_t rows, int64_t C,
+                      int dtype, float eps, void* stream);
+/* RMSNorm backward (no reference counterpart: the reference has only the torch
+ * autograd of reference/varlen_rmsnorm.py:50-57).  dx (rows, C) dtype; dweight
+ * (C,) fp32 or NULL.  Needs scree_norm_bwd_workspace_size() bytes of workspace
+ * when dweight != NULL. */
+size_t scree_norm_bwd_workspace_size(int64_t rows, int64_t C);
+int scree_rmsnorm_bwd(const void* dy, const void* x, const void* weight, int w_dtype,
+                      const float* rstd, void* dx, float* dweight, int64_t rows, int64_t C,
+                      int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* LayerNorm forward (biased variance).
+ * Replaces: scree/kernels/triton/varlen_layernorm.py:52-109 varlen_layernorm_triton
+ * (kernel :14-49); numerics follow reference/varlen_layernorm.py:64-74.
+ * mean, rstd: (rows,) fp32 or NULL. */
+int scree_layernorm_fwd(const void* x, int64_t x_row_stride, const void* weight,
+                        const void* bias, int w_dtype, void* y, int64_t y_row_stride,
+                        float* mean, float* rstd, int64_t rows, int64_t C, int dtype, float eps,
+                        void* stream);
+/* LayerNorm backward (new: reference relies on torch autograd of
+ * reference/varlen_layernorm.py:53-63).  dweight / dbias (C,) fp32 or NULL. */
+int scree_layernorm_bwd(const void* dy, const void* x, const void* weight, int w_dtype,
+                        const float* mean, const float* rstd, void* dx, float* dweight,
+                        float* dbias, int64_t rows, int64_t C, int dtype, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------ gathers
+ * pack: concatenate B contiguous row-major sources along rows.
+ * Replaces: scree/_core.py:97-141 pack (torch branch :108-113, torch.cat).
+ * src_ptrs: device array of B source pointers; offsets: device (B+1,) row
+ * offsets (int64 when offs_is_i64); row_bytes = bytes of one row (prod of the
+ * feature dims x element size).  src_align: a power of two dividing every
+ * source address (e.g. 16 when all are 16-byte aligned).  dst: (T, ...)
+ * contiguous. */
+int scree_pack(const void* const* src_ptrs, const void* offsets, int offs_is_i64, int64_t B,
+               int64_t T, int64_t row_bytes, int64_t src_align, void* dst, void* stream);
+
+/* to_padded: (T, ...) packed -> (B, max_len, ...) padded + (B, max_len) mask.
+ * Replaces: scree/_core.py:161-250 to_padded (torch branch :224-250).
+ * side_left = 0 pads on the right, 1 on the left.  fill_pattern: host pointer
+ * to elem_bytes bytes holding fill_value in the values' dtype.  mask: bool
+ * (1 byte per entry) or NULL. */
+int scree_to_padded(const void* values, const void* offsets, int offs_is_i64, int64_t B,
+                    int64_t max_len, int64_t row_bytes, int64_t elem_bytes,
+                    const void* fill_pattern_host, int side_left, void* padded, uint8_t* mask,
+                    void* stream);
+
+/* from_padded, step 1: per-row lengths = mask.sum(1) and int32 offsets (B+1,).
+ * Replaces: scree/_core.py:253-301 from_padded (torch branch :260-267), which
+ * assumes right padding. */
+int scree_padded_lengths(const uint8_t* mask, int64_t B, int64_t max_len, int32_t* offsets_out,
+                         void* stream);
+/* from_padded, step 2: gather the first lengths[b] rows of each padded row into
+ * the packed (T, ...) buffer, using the offsets from step 1. */
+int scree_from_padded(const void* padded, const int32_t* offsets, int64_t B, int64_t max_len,
+                      int64_t T, int64_t row_bytes, void* values, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SCREE_B200_H_ */

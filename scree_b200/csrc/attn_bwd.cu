@@ -1,0 +1,674 @@
+// attn_bwd.cu — varlen self-attention backward on sm_100a tensor cores.
+//
+// Gradients of O = softmax(Q K^T * scale) V per sequence and head, recomputing
+// P from the saved LSE (the FlashAttention-2 scheme that
+// scree/kernels/triton/_backward.py:73-285 also follows):
+//   P  = exp(S - LSE),  dV = P^T dO,  dP = dO V^T,
+//   dS = P * (dP - Delta),  Delta = rowsum(O * dO)   (_backward.py:37-69)
+//   dK = scale * dS^T Q,    dQ = scale * dS K
+// Five GEMMs per (key tile, query tile) pair, none recomputed.
+//
+// One CTA owns a 128-key tile of one head (K, V resident in shared memory) and
+// loops over the sequence's query tiles of BQ rows:
+//   warp 8    TMA: K, V once; Q_i, dO_i into a ring
+//   warp 9    MMA: S^T = K Q_i^T, dP^T = V dO_i^T, dV += P^T dO_i,
+//                  dK += dS^T Q_i, dQ_i (see below)
+//   warps 0-3 thread = key row = TMEM lane: P^T, dS^T from S^T, dP^T
+//   warps 4-7 read dQ_i from TMEM and add it into an fp32 accumulator in global
+//             memory with vector reductions; a final kernel casts it to q's dtype.
+// Two shapes:
+//   D = 128: BQ = 64 and dQ_i^T = K^T dS^T (M = D = 128 lanes, N = 64 queries),
+//            so each warp's reductions cover 32 consecutive features (128 B);
+//   D <= 64: BQ = 128 and dQ_i = dS K (M = 128 queries, N = D).
+// TMEM columns: S^T [0,BQ), dP^T [BQ,2BQ), dV [2BQ,2BQ+D), dK [.., +D), dQ [.., +BQ or D).
+#include <algorithm>
+#include "attn_common.cuh"
+
+namespace scree {
+namespace {
+
+constexpr int BN = 128;  // keys per CTA
+constexpr int kThreads = 320;
+
+template <int D>
+struct BwdCfg {
+  static constexpr bool DQT = (D == 128);
+  static constexpr int BQ = DQT ? 64 : 128;
+  static constexpr int SWB = D >= 64 ? 128 : 64;
+  static constexpr int CHUNK = SWB / 2;
+  static constexpr int NCHUNK = D / CHUNK;
+  static constexpr uint32_t SWZ = SWB == 128 ? SW_128B : SW_64B;
+  static constexpr int STAGES = 2;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int QT_BYTES = BQ * D * 2;
+  static constexpr int PT_BYTES = BN * BQ * 2;
+  static constexpr int OFF_K = 0;
+  static constexpr int OFF_V = OFF_K + KV_BYTES;
+  static constexpr int OFF_Q = OFF_V + KV_BYTES;
+  static constexpr int OFF_DO = OFF_Q + STAGES * QT_BYTES;
+  static constexpr int OFF_PT = OFF_DO + STAGES * QT_BYTES;
+  static constexpr int OFF_DS = OFF_PT + PT_BYTES;
+  static constexpr int OFF_LD = OFF_DS + PT_BYTES;          // lse2 / delta [2][2][BQ] fp32
+  static constexpr int OFF_BAR = OFF_LD + 2 * 2 * BQ * 4;
+  // At least 120 KB so two CTAs (each holding all 512 TMEM columns) never share an SM.
+  static constexpr int SMEM_RAW = OFF_BAR + 512 + 1024;
+  static constexpr int SMEM = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
+  static constexpr int COL_S = 0, COL_DP = BQ, COL_DV = 2 * BQ, COL_DK = 2 * BQ + D,
+                       COL_DQ = 2 * BQ + 2 * D;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(COL_DQ + (DQT ? BQ : D) <= TMEM_COLS, "TMEM budget");
+};
+
+struct BwdParams {
+  const void* offs;
+  int is64;
+  int H;
+  int T;
+  float scale;       // softmax scale
+  float scale_log2;  // scale * log2(e)
+  const int32_t* tile_count;
+  const TileRef* tiles;
+  int* status;  // device status word
+  const float* lse2T;   // [H][T], lse * log2(e)
+  const float* deltaT;  // [H][T]
+  float* dq_acc;        // [T][H][D] fp32
+  void* dk;
+  void* dv;
+};
+
+template <int D>
+__device__ __forceinline__ uint64_t kmaj(uint32_t base, int rows, int kk) {
+  using C = BwdCfg<D>;
+  const int e = kk * 16;
+  return make_sdesc(base + (e / C::CHUNK) * rows * C::SWB + (e % C::CHUNK) * 2, 16, 8 * C::SWB,
+                    C::SWZ);
+}
+// MN-major view of a [rows][D] TMA tile, K dimension = rows (16 per k-step).
+template <int D>
+__device__ __forceinline__ uint64_t mnmaj(uint32_t base, int rows, int kk) {
+  using C = BwdCfg<D>;
+  return make_sdesc(base + kk * 16 * C::SWB, rows * C::SWB, 8 * C::SWB, C::SWZ);
+}
+// P^T / dS^T tile [BN keys][BQ queries], 64-query 128B-swizzled column blocks.
+// K-major view with K = queries:
+__device__ __forceinline__ uint64_t pt_kmaj(uint32_t base, int kk) {
+  const int e = kk * 16;
+  return make_sdesc(base + (e / 64) * BN * 128 + (e % 64) * 2, 16, 1024, SW_128B);
+}
+// MN-major view with K = keys (16 rows per step), MN = queries:
+__device__ __forceinline__ uint64_t pt_mnmaj(uint32_t base, int kk) {
+  return make_sdesc(base + kk * 16 * 128, BN * 128, 1024, SW_128B);
+}
+
+template <typename T> struct Pk2b;
+template <> struct Pk2b<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct Pk2b<__half> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+// Named barrier over the 128 threads of warps 0-3.
+__device__ __forceinline__ void softmax_group_sync() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+// Row-major [BN][BQ] 16-bit tile in 128B swizzle: write the BQ values of row kr.
+template <typename T, int BQ>
+__device__ __forceinline__ void write_row_sw128(uint8_t* base, int kr, const float* v) {
+  const int sw = kr & 7;
+#pragma unroll
+  for (int u = 0; u < BQ / 8; ++u) {
+    uint4 w;
+    w.x = Pk2b<T>::pack(v[u * 8 + 0], v[u * 8 + 1]);
+    w.y = Pk2b<T>::pack(v[u * 8 + 2], v[u * 8 + 3]);
+    w.z = Pk2b<T>::pack(v[u * 8 + 4], v[u * 8 + 5]);
+    w.w = Pk2b<T>::pack(v[u * 8 + 6], v[u * 8 + 7]);
+    const int blk = u >> 3, uu = u & 7;
+    *reinterpret_cast<uint4*>(base + blk * BN * 128 + kr * 128 + ((uu ^ sw) << 4)) = w;
+  }
+}
+
+template <int D, typename T, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                    const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v,
+                    const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+  using C = BwdCfg<D>;
+  constexpr int BQ = C::BQ;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t ID_S = make_idesc_f16(BN, BQ, kBF16, false, false);
+  constexpr uint32_t ID_ACC = make_idesc_f16(BN, D, kBF16, false, true);
+  constexpr uint32_t ID_DQ = C::DQT ? make_idesc_f16(D, BQ, kBF16, true, true)
+                                    : make_idesc_f16(BQ, D, kBF16, true, true);
+
+  const int item = blockIdx.x;
+  const int ntiles = *p.tile_count;
+  if (item >= ntiles * p.H) return;
+  // A CTA of an earlier failed launch (or of this one) set the status word: skip.
+  if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
+  const TileRef tr = p.tiles[item / p.H];
+  const int h = item % p.H;
+  const int64_t row0 = load_offset(p.offs, p.is64, tr.seq);
+  const int L = (int)(load_offset(p.offs, p.is64, tr.seq + 1) - row0);
+  const int k0 = tr.tile * BN;
+  const int nq = (L + BQ - 1) / BQ;
+  const int i_first = CAUSAL ? k0 / BQ : 0;
+  const int n_it = nq - i_first;  // >= 1 since k0 < L
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sK = smem_u32(smem + C::OFF_K), sV = smem_u32(smem + C::OFF_V);
+  const uint32_t sQ = smem_u32(smem + C::OFF_Q), sDO = smem_u32(smem + C::OFF_DO);
+  const uint32_t sPT = smem_u32(smem + C::OFF_PT), sDS = smem_u32(smem + C::OFF_DS);
+  float* lds = reinterpret_cast<float*>(smem + C::OFF_LD);  // [buf][0 lse | 1 delta][BQ]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;               // [STAGES]
+  uint64_t* q_empty = q_full + C::STAGES;    // [STAGES]
+  uint64_t* s_full = q_empty + C::STAGES;
+  uint64_t* dp_full = s_full + 1;
+  uint64_t* p_full = dp_full + 1;
+  uint64_t* ds_full = p_full + 1;
+  uint64_t* p_free = ds_full + 1;
+  uint64_t* ds_free = p_free + 1;
+  uint64_t* dq_full = ds_free + 1;
+  uint64_t* dq_empty = dq_full + 1;
+  uint64_t* acc_done = dq_empty + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(ds_full, 128);
+    mbar_init(p_free, 1);
+    mbar_init(ds_free, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 128);
+    mbar_init(acc_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) tmem_alloc<C::TMEM_COLS>(tmem_slot);
+  if (warp == 8 && (threadIdx.x & 31) == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+    tma_prefetch_desc(&tm_do);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
+#pragma unroll
+      for (int c = 0; c < C::NCHUNK; ++c) {
+        tma_load_3d(smem + C::OFF_K + c * BN * C::SWB, &tm_k, kv_full, c * C::CHUNK, h,
+                    (int)row0 + k0);
+        tma_load_3d(smem + C::OFF_V + c * BN * C::SWB, &tm_v, kv_full, c * C::CHUNK, h,
+                    (int)row0 + k0);
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int st = it % C::STAGES;
+        if (it >= C::STAGES &&
+            !mbar_wait(&q_empty[st], ((it / C::STAGES) - 1) & 1, abort_flag, p.status, 21))
+          break;
+        const int qrow = (int)row0 + (i_first + it) * BQ;
+        mbar_expect_tx(&q_full[st], 2 * C::QT_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::NCHUNK; ++c) {
+          tma_load_3d(smem + C::OFF_Q + st * C::QT_BYTES + c * BQ * C::SWB, &tm_q, &q_full[st],
+                      c * C::CHUNK, h, qrow);
+          tma_load_3d(smem + C::OFF_DO + st * C::QT_BYTES + c * BQ * C::SWB, &tm_do,
+                      &q_full[st], c * C::CHUNK, h, qrow);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 22) && mbar_wait(&q_full[0], 0, abort_flag, p.status, 23);
+      auto issue_s_dp = [&](int it, bool s_part) {
+        const int st = it % C::STAGES;
+        if (s_part) {
+          const uint32_t qb = sQ + st * C::QT_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_f16_ss(tmem + C::COL_S, kmaj<D>(sK, BN, kk), kmaj<D>(qb, BQ, kk), ID_S,
+                        kk > 0 ? 1u : 0u);
+          umma_commit(s_full);
+        } else {
+          const uint32_t ob = sDO + st * C::QT_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            umma_f16_ss(tmem + C::COL_DP, kmaj<D>(sV, BN, kk), kmaj<D>(ob, BQ, kk), ID_S,
+                        kk > 0 ? 1u : 0u);
+          umma_commit(dp_full);
+        }
+      };
+      if (ok) {
+        tc_fence_after();
+        issue_s_dp(0, true);
+        issue_s_dp(0, false);
+      }
+      for (int it = 0; ok && it < n_it; ++it) {
+        const int st = it % C::STAGES;
+        const uint32_t qb = sQ + st * C::QT_BYTES, ob = sDO + st * C::QT_BYTES;
+        // dV += P^T dO_i
+        if (!(ok = mbar_wait(p_full, it & 1, abort_flag, p.status, 24))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          umma_f16_ss(tmem + C::COL_DV, pt_kmaj(sPT, kk), mnmaj<D>(ob, BQ, kk), ID_ACC,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(p_free);
+        // S^T for the next query tile overlaps the softmax warps' dS work.
+        const bool more = it + 1 < n_it;
+        if (more) {
+          const int st1 = (it + 1) % C::STAGES;
+          if (!(ok = mbar_wait(&q_full[st1], ((it + 1) / C::STAGES) & 1, abort_flag, p.status, 25))) break;
+          tc_fence_after();
+          issue_s_dp(it + 1, true);
+        }
+        // dK += dS^T Q_i ; dQ_i
+        if (!(ok = mbar_wait(ds_full, it & 1, abort_flag, p.status, 26))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk)
+          umma_f16_ss(tmem + C::COL_DK, pt_kmaj(sDS, kk), mnmaj<D>(qb, BQ, kk), ID_ACC,
+                      (it > 0 || kk > 0) ? 1u : 0u);
+        if (it > 0 && !(ok = mbar_wait(dq_empty, (it - 1) & 1, abort_flag, p.status, 27))) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          if (C::DQT)  // dQ^T = K^T dS^T : A = K (MN-major, M = D), B = dS^T (MN-major, N = q)
+            umma_f16_ss(tmem + C::COL_DQ, mnmaj<D>(sK, BN, kk), pt_mnmaj(sDS, kk), ID_DQ,
+                        kk > 0 ? 1u : 0u);
+          else         // dQ = dS K : A = dS (MN-major, M = q), B = K (MN-major, N = D)
+            umma_f16_ss(tmem + C::COL_DQ, pt_mnmaj(sDS, kk), mnmaj<D>(sK, BN, kk), ID_DQ,
+                        kk > 0 ? 1u : 0u);
+        }
+        umma_commit(dq_full);
+        umma_commit(ds_free);
+        umma_commit(&q_empty[st]);
+        if (more) issue_s_dp(it + 1, false);
+      }
+      umma_commit(acc_done);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------------------------ P^T / dS^T
+    const int kr = threadIdx.x;  // key row within the tile == TMEM lane
+    const int kidx = k0 + kr;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool key_ok = kidx < L;
+    const float sl2 = p.scale_log2;
+    const float* lse_h = p.lse2T + (int64_t)h * p.T + row0;
+    const float* del_h = p.deltaT + (int64_t)h * p.T + row0;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (i_first + it) * BQ;
+      float* lse_s = lds + (it & 1) * 2 * BQ;
+      float* del_s = lse_s + BQ;
+      // Stage this tile's LSE and Delta (queries past L read as 0; masked below).
+      if (kr < BQ) {
+        const int q = q0 + kr;
+        lse_s[kr] = q < L ? lse_h[q] : 0.f;
+      } else {
+        const int q = q0 + kr - BQ;
+        if (kr - BQ < BQ) del_s[kr - BQ] = q < L ? del_h[q] : 0.f;
+      }
+      if (BQ == 128) {  // 128 threads, 2 x 128 values: second half
+        const int q = q0 + kr;
+        del_s[kr] = q < L ? del_h[q] : 0.f;
+      }
+      softmax_group_sync();
+      const bool need_mask = (q0 + BQ > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
+      // ---- P^T row from S^T
+      ok = mbar_wait(s_full, it & 1, abort_flag, p.status, 28);
+      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+      tc_fence_after();
+      float pr[BQ];
+#pragma unroll
+      for (int c = 0; c < BQ / 32; ++c)
+        tmem_ld32(lane_base + C::COL_S + c * 32, *reinterpret_cast<float(*)[32]>(&pr[c * 32]));
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < BQ; ++c) {
+        float x = ex2_approx(fmaf(pr[c], sl2, -lse_s[c]));
+        if (need_mask) {
+          const int q = q0 + c;
+          const bool valid = key_ok && q < L && (!CAUSAL || q >= kidx);
+          x = valid ? x : 0.f;
+        }
+        pr[c] = x;
+      }
+      if (it > 0) {
+        ok = mbar_wait(p_free, (it - 1) & 1, abort_flag, p.status, 29);
+        if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+      }
+      write_row_sw128<T, BQ>(smem + C::OFF_PT, kr, pr);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      // ---- dS^T = P^T * (dP^T - Delta)
+      ok = mbar_wait(dp_full, it & 1, abort_flag, p.status, 30);
+      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < BQ / 32; ++c) {
+        float dp[32];
+        tmem_ld32(lane_base + C::COL_DP + c * 32, dp);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pr[c * 32 + e] *= (dp[e] - del_s[c * 32 + e]);
+      }
+      if (it > 0) {
+        ok = mbar_wait(ds_free, (it - 1) & 1, abort_flag, p.status, 31);
+        if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+      }
+      write_row_sw128<T, BQ>(smem + C::OFF_DS, kr, pr);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+    }
+    // ---- dK, dV epilogue
+    if (ok) {
+      ok = mbar_wait(acc_done, 0, abort_flag, p.status, 32);
+      ok = __all_sync(0xffffffff, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      T* dvrow = reinterpret_cast<T*>(p.dv) + ((row0 + kidx) * p.H + h) * D;
+      T* dkrow = reinterpret_cast<T*>(p.dk) + ((row0 + kidx) * p.H + h) * D;
+#pragma unroll
+      for (int pass = 0; pass < 2; ++pass) {
+        const int col = pass == 0 ? C::COL_DV : C::COL_DK;
+        const float mul = pass == 0 ? 1.f : p.scale;
+        T* dst = pass == 0 ? dvrow : dkrow;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(lane_base + col + c * 32, v);
+          tmem_wait_ld();
+          if (key_ok) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              uint4 w;
+              w.x = Pk2b<T>::pack(v[u * 8 + 0] * mul, v[u * 8 + 1] * mul);
+              w.y = Pk2b<T>::pack(v[u * 8 + 2] * mul, v[u * 8 + 3] * mul);
+              w.z = Pk2b<T>::pack(v[u * 8 + 4] * mul, v[u * 8 + 5] * mul);
+              w.w = Pk2b<T>::pack(v[u * 8 + 6] * mul, v[u * 8 + 7] * mul);
+              *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = w;
+            }
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dQ reduction warps 4-7
+    const int ln = threadIdx.x - 128;  // TMEM lane: feature d (DQT) or query row
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+    const float sc = p.scale;
+    for (int it = 0; it < n_it; ++it) {
+      const int q0 = (i_first + it) * BQ;
+      bool ok = mbar_wait(dq_full, it & 1, abort_flag, p.status, 33);
+      if (!__all_sync(0xffffffff, ok)) break;
+      tc_fence_after();
+      if (C::DQT) {
+        float v[BQ];
+#pragma unroll
+        for (int c = 0; c < BQ / 32; ++c)
+          tmem_ld32(lane_base + C::COL_DQ + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(dq_empty);
+        const int qmax = min(BQ, L - q0);
+        float* base = p.dq_acc + ((row0 + q0) * p.H + h) * D + ln;
+        const int64_t rstride = (int64_t)p.H * D;
+#pragma unroll 8
+        for (int c = 0; c < BQ; ++c)
+          if (c < qmax) atomicAdd(base + c * rstride, v[c] * sc);
+      } else {
+        const int q = q0 + ln;
+        float* base = p.dq_acc + ((row0 + q) * p.H + h) * D;
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          float v[32];
+          tmem_ld32(lane_base + C::COL_DQ + c * 32, v);
+          tmem_wait_ld();
+          if (q < L) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              red_add_v4(base + c * 32 + u * 4, v[u * 4] * sc, v[u * 4 + 1] * sc,
+                         v[u * 4 + 2] * sc, v[u * 4 + 3] * sc);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(dq_empty);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc<C::TMEM_COLS>(tmem);
+  }
+}
+
+// Delta[h][t] = sum_d O[t,h,d] * dO[t,h,d] (fp32) and lse2T[h][t] = lse[t,h] * log2(e).
+// 8 threads per (t, h) row, 16-byte loads.
+template <typename T, int D>
+__global__ void bwd_preprocess_kernel(const T* __restrict__ o, const T* __restrict__ dout,
+                                      const float* __restrict__ lse, int64_t T_, int H,
+                                      float* __restrict__ deltaT, float* __restrict__ lse2T) {
+  constexpr int TPR = 8;
+  constexpr int EPT = D / TPR;  // elements per thread (4, 8 or 16)
+  const int64_t nrows = T_ * H;
+  const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t row = gid / TPR;
+  const int sub = (int)(gid % TPR);
+  float acc = 0.f;
+  if (row < nrows) {
+    const T* op = o + row * D + sub * EPT;
+    const T* dp = dout + row * D + sub * EPT;
+#pragma unroll
+    for (int e = 0; e < EPT; e += 4) {
+      const uint2 a = *reinterpret_cast<const uint2*>(op + e);
+      const uint2 b = *reinterpret_cast<const uint2*>(dp + e);
+      const T* ah = reinterpret_cast<const T*>(&a);
+      const T* bh = reinterpret_cast<const T*>(&b);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) acc += Cvt<T>::to_f(ah[k]) * Cvt<T>::to_f(bh[k]);
+    }
+  }
+#pragma unroll
+  for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, off);
+  if (row < nrows && sub == 0) {
+    const int64_t t = row / H;
+    const int hh = (int)(row % H);
+    deltaT[(int64_t)hh * T_ + t] = acc;
+    lse2T[(int64_t)hh * T_ + t] = lse[row] * 1.4426950408889634f;
+  }
+}
+
+// dq (dtype) = dq_acc (fp32), 4 elements per thread.
+template <typename T>
+__global__ void cast_dq_kernel(const float* __restrict__ acc, T* __restrict__ dq, int64_t n4) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4*>(acc)[i];
+    uint2 w;
+    w.x = Pk2b<T>::pack(v.x, v.y);
+    w.y = Pk2b<T>::pack(v.z, v.w);
+    reinterpret_cast<uint2*>(dq)[i] = w;
+  }
+}
+
+template <int D, typename T, bool CAUSAL>
+int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+               const CUtensorMap& tdo, const BwdParams& p, int64_t grid, cudaStream_t s) {
+  auto kern = attn_bwd_kernel<D, T, CAUSAL>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    SCREE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        BwdCfg<D>::SMEM));
+    attr_set[dev & 63] = true;
+  }
+  ProfScope prof(PROF_ATTN_BWD, s);
+  kern<<<(unsigned)grid, kThreads, BwdCfg<D>::SMEM, s>>>(tq, tk, tv, tdo, p);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+struct BwdWs {
+  size_t off_dq, off_delta, off_lse2, off_sched, total;
+};
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+BwdWs bwd_ws_layout(int64_t B, int64_t T, int64_t H, int D) {
+  BwdWs w;
+  w.off_dq = 0;
+  w.off_delta = align256(w.off_dq + (size_t)T * H * D * 4);
+  w.off_lse2 = align256(w.off_delta + (size_t)T * H * 4);
+  w.off_sched = align256(w.off_lse2 + (size_t)T * H * 4);
+  w.total = w.off_sched + schedule_bytes(B, T, BN);
+  return w;
+}
+
+template <typename T>
+int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v, const void* o,
+                  const float* lse, const void* offsets, int is64, int64_t B, int64_t Tn, int64_t H,
+                  int D, int causal, float scale, void* dq, void* dk, void* dv, char* ws,
+                  const BwdWs& L, cudaStream_t s) {
+  constexpr bool bf16 = std::is_same<T, __nv_bfloat16>::value;
+  const int swb = D >= 64 ? 128 : 64;
+  const int bq = D == 128 ? 64 : 128;
+  CUtensorMap tq, tk, tv, tdo;
+  int rc;
+  const int64_t rs = H * D, hs = D;
+  if ((rc = make_thd_map(&tq, q, Tn, H, D, rs, hs, swb / 2, bq, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tdo, dout, Tn, H, D, rs, hs, swb / 2, bq, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tk, k, Tn, H, D, rs, hs, swb / 2, BN, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tv, v, Tn, H, D, rs, hs, swb / 2, BN, swb, bf16))) return rc;
+
+  float* dq_acc = reinterpret_cast<float*>(ws + L.off_dq);
+  float* deltaT = reinterpret_cast<float*>(ws + L.off_delta);
+  float* lse2T = reinterpret_cast<float*>(ws + L.off_lse2);
+  void* sched = ws + L.off_sched;
+  SCREE_CUDA_TRY(cudaMemsetAsync(dq_acc, 0, (size_t)Tn * H * D * 4, s));
+  {
+    const int64_t threads = Tn * H * 8;
+    const unsigned blocks = (unsigned)((threads + 255) / 256);
+    if (D == 128) bwd_preprocess_kernel<T, 128><<<blocks, 256, 0, s>>>((const T*)o, (const T*)dout, lse, Tn, (int)H, deltaT, lse2T);
+    else if (D == 64) bwd_preprocess_kernel<T, 64><<<blocks, 256, 0, s>>>((const T*)o, (const T*)dout, lse, Tn, (int)H, deltaT, lse2T);
+    else bwd_preprocess_kernel<T, 32><<<blocks, 256, 0, s>>>((const T*)o, (const T*)dout, lse, Tn, (int)H, deltaT, lse2T);
+    SCREE_LAUNCH_CHECK();
+  }
+  if ((rc = launch_build_schedule(offsets, is64, B, BN, bq, causal, 1, sched, s))) return rc;
+  BwdParams p;
+  p.offs = offsets;
+  p.is64 = is64;
+  p.H = (int)H;
+  p.T = (int)Tn;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.tile_count = reinterpret_cast<const int32_t*>(sched);
+  p.status = device_status_ptr();
+  p.tiles = reinterpret_cast<const TileRef*>((const char*)sched + 16);
+  p.lse2T = lse2T;
+  p.deltaT = deltaT;
+  p.dq_acc = dq_acc;
+  p.dk = dk;
+  p.dv = dv;
+  const int64_t grid = max_tiles(B, Tn, BN) * H;
+  if (grid >= (1ll << 31)) {
+    set_last_error("attn_bwd: grid too large");
+    return SCREE_ERR_INVALID;
+  }
+#define SCREE_BWD_CASE(DD)                                                        \
+  if (D == DD) {                                                                  \
+    rc = causal ? launch_bwd<DD, T, true>(tq, tk, tv, tdo, p, grid, s)            \
+                : launch_bwd<DD, T, false>(tq, tk, tv, tdo, p, grid, s);          \
+  }
+  SCREE_BWD_CASE(128)
+  SCREE_BWD_CASE(64)
+  SCREE_BWD_CASE(32)
+#undef SCREE_BWD_CASE
+  if (rc) return rc;
+  const int64_t n4 = Tn * H * D / 4;
+  const unsigned cgrid = (unsigned)std::min<int64_t>((n4 + 255) / 256, (int64_t)num_sms() * 16);
+  cast_dq_kernel<T><<<cgrid, 256, 0, s>>>(dq_acc, (T*)dq, n4);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+}  // namespace
+}  // namespace scree
+
+using namespace scree;
+
+extern "C" size_t scree_attn_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int D) {
+  return bwd_ws_layout(B, T, H, D).total;
+}
+
+extern "C" int scree_attn_bwd(const void* dout, const void* q, const void* k, const void* v,
+                              const void* o, const float* lse, const void* offsets,
+                              int offs_is_i64, int64_t B, int64_t T, int64_t H, int D, int dtype,
+                              int causal, float scale, int64_t max_seqlen, void* dq, void* dk,
+                              void* dv, void* workspace, size_t workspace_bytes, void* stream) {
+  (void)max_seqlen;
+  SCREE_CHECK_ARG(B >= 1 && T >= 0 && H >= 1, "attn_bwd: bad sizes");
+  SCREE_CHECK_ARG(T < (1ll << 31) && H < 65536, "attn_bwd: T or H too large");
+  if (D != 32 && D != 64 && D != 128) {
+    set_last_error("attn_bwd: head_dim %d unsupported (32, 64, 128)", D);
+    return SCREE_ERR_UNSUPPORTED;
+  }
+  SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16, "attn_bwd: fp16 or bf16 only");
+  if (T == 0) return SCREE_OK;
+  SCREE_CHECK_ARG(dout && q && k && v && o && lse && offsets && dq && dk && dv,
+                  "attn_bwd: null pointer");
+  const BwdWs L = bwd_ws_layout(B, T, H, D);
+  SCREE_CHECK_ARG(workspace && workspace_bytes >= L.total,
+                  "attn_bwd: workspace too small (%zu < %zu)", workspace_bytes, L.total);
+  const void* ptrs[8] = {dout, q, k, v, o, dq, dk, dv};
+  for (const void* ptr : ptrs)
+    SCREE_CHECK_ARG(((uintptr_t)ptr % 16) == 0, "attn_bwd: tensors must be 16-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  char* ws = reinterpret_cast<char*>(workspace);
+  if (dtype == SCREE_BF16)
+    return run_bwd_typed<__nv_bfloat16>(dout, q, k, v, o, lse, offsets, offs_is_i64, B, T, H, D,
+                                        causal, scale, dq, dk, dv, ws, L, s);
+  return run_bwd_typed<__half>(dout, q, k, v, o, lse, offsets, offs_is_i64, B, T, H, D, causal,
+                               scale, dq, dk, dv, ws, L, s);
+}

@@ -1,0 +1,455 @@
+// attn_fwd.cu — varlen self-attention forward on sm_100a tensor cores.
+//
+// Computes, per sequence b and head h (reference/varlen_attention.py:121-138):
+//   S = Q K^T * scale, causal mask k > q -> -inf, P = softmax(S), O = P V,
+//   LSE = m + ln(l)  (natural log; triton/varlen_attention.py:160)
+// One CTA owns one 128-row query tile of one head and streams the sequence's
+// 128-key tiles through a TMA -> tcgen05.mma pipeline:
+//
+//   warp 4  (TMA)      Q once; K_j, V_j into a STAGES-deep ring (mbarrier tx)
+//   warp 5  (MMA)      S_j = Q K_j^T into TMEM buffer j%2, then O += P_{j-1} V_{j-1}
+//   warps 0-3 (softmax) thread r owns query row r == TMEM lane r: reads S_j,
+//                      masks, keeps running max/sum in registers, writes P_j
+//                      (bf16/fp16, 128B-swizzled K-major) to shared memory,
+//                      rescales O in TMEM only when the max grew by more than
+//                      2^8 (exact: P stays <= 256), and finally writes O / l, LSE.
+//
+// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).
+// Softmax works in the exp2 domain with log2(e) folded into the scale.
+// Ragged tails: TMA reads whole 128-row boxes, so rows of the next sequence
+// arrive in K/V tiles; keys >= L are masked to -inf (P = 0), and query rows
+// >= L are computed but never stored.  Rows past T are zero-filled by TMA.
+#include "attn_common.cuh"
+
+namespace scree {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int kThreads = 192;
+
+template <int D>
+struct FwdCfg {
+  static constexpr int SWB = D >= 64 ? 128 : 64;  // swizzle span in bytes (one smem row)
+  static constexpr int CHUNK = SWB / 2;           // elements per swizzle row
+  static constexpr int NCHUNK = D / CHUNK;
+  static constexpr uint32_t SWZ = SWB == 128 ? SW_128B : SW_64B;
+  static constexpr int STAGES = D == 128 ? 2 : 3;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  // barriers + alignment slack; at least 120 KB so that two CTAs (each holding
+  // all 512 TMEM columns) never share an SM.
+  static constexpr int SMEM_RAW = OFF_BAR + 256 + 1024;
+  static constexpr int SMEM = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
+};
+
+struct FwdParams {
+  const void* offs;
+  int is64;
+  int H;
+  int T;
+  float scale_log2;
+  const int32_t* tile_count;
+  const TileRef* tiles;
+  int* status;  // device status word
+  void* o;
+  int64_t o_rs, o_hs;
+  float* lse;
+};
+
+// K-major operand descriptor for k-step `kk` (16 elements) of a [rows][D] tile
+// stored as NCHUNK column blocks of [rows][SWB bytes].
+template <int D>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int rows, int kk) {
+  using C = FwdCfg<D>;
+  const int e = kk * 16;
+  const uint32_t addr = base + (e / C::CHUNK) * rows * C::SWB + (e % C::CHUNK) * 2;
+  return make_sdesc(addr, 16, 8 * C::SWB, C::SWZ);
+}
+// P tile: [BM][BN] with 64-key 128-byte swizzled column blocks.
+__device__ __forceinline__ uint64_t p_desc(uint32_t base, int kk) {
+  const int e = kk * 16;
+  const uint32_t addr = base + (e / 64) * BM * 128 + (e % 64) * 2;
+  return make_sdesc(addr, 16, 1024, SW_128B);
+}
+// V as the MN-major B operand (N = D, K = keys): k-step kk covers keys
+// [16kk, 16kk+16) = 16 smem rows; D-chunks are BN*SWB bytes apart (LBO), groups of
+// 8 keys are 8*SWB apart (SBO).
+template <int D>
+__device__ __forceinline__ uint64_t v_desc(uint32_t base, int kk) {
+  using C = FwdCfg<D>;
+  return make_sdesc(base + kk * 16 * C::SWB, BN * C::SWB, 8 * C::SWB, C::SWZ);
+}
+
+template <typename T> struct Pk2;
+template <> struct Pk2<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+template <> struct Pk2<__half> {
+  static __device__ __forceinline__ uint32_t pack(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+};
+
+template <int D, typename T, bool CAUSAL>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                    const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+  using C = FwdCfg<D>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_S = make_idesc_f16(BM, BN, kBF16, false, false);
+  constexpr uint32_t IDESC_O = make_idesc_f16(BM, D, kBF16, false, true);
+
+  const int item = blockIdx.x;
+  const int ntiles = *p.tile_count;
+  if (item >= ntiles * p.H) return;
+  // A CTA of an earlier failed launch (or of this one) set the status word: skip.
+  if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
+  const TileRef tr = p.tiles[item / p.H];
+  const int h = item % p.H;
+  const int64_t seq_start = load_offset(p.offs, p.is64, tr.seq);
+  const int L = (int)(load_offset(p.offs, p.is64, tr.seq + 1) - seq_start);
+  const int q0 = tr.tile * BM;
+  const int nk_all = (L + BN - 1) / BN;
+  const int n_kv = CAUSAL ? min(nk_all, (q0 + BM - 1) / BN + 1) : nk_all;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const uint32_t sQ = smem_u32(smem + C::OFF_Q);
+  const uint32_t sK = smem_u32(smem + C::OFF_K);
+  const uint32_t sV = smem_u32(smem + C::OFF_V);
+  const uint32_t sP = smem_u32(smem + C::OFF_P);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;                  // [STAGES]
+  uint64_t* v_full = k_full + C::STAGES;        // [STAGES]
+  uint64_t* kv_empty = v_full + C::STAGES;      // [STAGES]
+  uint64_t* s_full = kv_empty + C::STAGES;      // [2]
+  uint64_t* s_empty = s_full + 2;               // [2]
+  uint64_t* p_full = s_empty + 2;               // [2]
+  uint64_t* pv_done = p_full + 2;               // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_empty[b], 128);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&pv_done[b], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) tmem_alloc<512>(tmem_slot);
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one()) {
+      const int row0 = (int)seq_start;
+      mbar_expect_tx(q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < C::NCHUNK; ++c)
+        tma_load_3d(smem + C::OFF_Q + c * BM * C::SWB, &tm_q, q_full, c * C::CHUNK, h, row0 + q0);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::STAGES;
+        if (j >= C::STAGES &&
+            !mbar_wait(&kv_empty[st], ((j / C::STAGES) - 1) & 1, abort_flag, p.status, 1))
+          break;
+        mbar_expect_tx(&k_full[st], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::NCHUNK; ++c)
+          tma_load_3d(smem + C::OFF_K + st * C::KV_BYTES + c * BN * C::SWB, &tm_k, &k_full[st],
+                      c * C::CHUNK, h, row0 + j * BN);
+        mbar_expect_tx(&v_full[st], C::KV_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::NCHUNK; ++c)
+          tma_load_3d(smem + C::OFF_V + st * C::KV_BYTES + c * BN * C::SWB, &tm_v, &v_full[st],
+                      c * C::CHUNK, h, row0 + j * BN);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      auto issue_pv = [&](int i) -> bool {
+        const int b2 = i & 1, st = i % C::STAGES;
+        if (!mbar_wait(&p_full[b2], (i >> 1) & 1, abort_flag, p.status, 2)) return false;
+        if (!mbar_wait(&v_full[st], (i / C::STAGES) & 1, abort_flag, p.status, 3)) return false;
+        tc_fence_after();
+        const uint32_t pb = sP + b2 * C::P_BYTES;
+        const uint32_t vb = sV + st * C::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16_ss(tmem + 256, p_desc(pb, kk), v_desc<D>(vb, kk), IDESC_O,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[b2]);
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 4);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int st = j % C::STAGES, b2 = j & 1;
+        if (!mbar_wait(&k_full[st], (j / C::STAGES) & 1, abort_flag, p.status, 5)) { ok = false; break; }
+        if (j >= 2 && !mbar_wait(&s_empty[b2], ((j - 2) >> 1) & 1, abort_flag, p.status, 6)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t kb = sK + st * C::KV_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16_ss(tmem + b2 * BN, kmajor_desc<D>(sQ, BM, kk), kmajor_desc<D>(kb, BN, kk),
+                      IDESC_S, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[b2]);
+        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+      }
+      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax warps
+    const int r = threadIdx.x;  // query row within the tile == TMEM lane
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const int qi = q0 + r;      // query index within the sequence
+    const float sl2 = p.scale_log2;
+    float m_used = -INFINITY;   // running max, scaled log2 units
+    float l = 0.f;
+    bool ok = true;
+    uint8_t* prow_base = smem + C::OFF_P + r * 128;
+    const int sw = r & 7;
+    for (int j = 0; j < n_kv; ++j) {
+      const int b2 = j & 1;
+      ok = mbar_wait(&s_full[b2], (j >> 1) & 1, abort_flag, p.status, 7);
+      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+      tc_fence_after();
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_ld32(lane_base + b2 * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[b2]);
+
+      const int k0 = j * BN;
+      const bool need_mask = (k0 + BN > L) || (CAUSAL && k0 + BN - 1 > q0);
+      if (need_mask) {
+        const int lim = CAUSAL ? min(L - 1, qi) : (L - 1);  // last valid key
+#pragma unroll
+        for (int c = 0; c < BN; ++c)
+          if (k0 + c > lim) s[c] = -INFINITY;
+      }
+      float mx = s[0];
+#pragma unroll
+      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      const float m_cand = mx * sl2;
+      float alpha = 1.f;
+      bool need = false;
+      if (m_used == -INFINITY) {
+        need = true;
+        alpha = 0.f;
+        m_used = m_cand;
+      } else if (m_cand > m_used + 8.0f) {
+        need = true;
+        alpha = ex2_approx(m_used - m_cand);
+        m_used = m_cand;
+      }
+      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        s[c] = ex2_approx(fmaf(s[c], sl2, -m_eff));
+        rs += s[c];
+      }
+      if (j >= 1) {
+        ok = mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status, 8);
+        if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffff, need)) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float o[32];
+            tmem_ld32(lane_base + 256 + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] *= alpha;
+            tmem_st32(lane_base + 256 + c * 32, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      l = l * alpha + rs;
+      // P row -> shared memory, 128B swizzle: 16-byte unit u of row r lives at
+      // unit position u ^ (r % 8) within its 128-byte row.
+      uint8_t* prow = prow_base + b2 * C::P_BYTES;
+#pragma unroll
+      for (int u = 0; u < BN / 8; ++u) {
+        uint4 w;
+        w.x = Pk2<T>::pack(s[u * 8 + 0], s[u * 8 + 1]);
+        w.y = Pk2<T>::pack(s[u * 8 + 2], s[u * 8 + 3]);
+        w.z = Pk2<T>::pack(s[u * 8 + 4], s[u * 8 + 5]);
+        w.w = Pk2<T>::pack(s[u * 8 + 6], s[u * 8 + 7]);
+        const int blk = u >> 3, uu = u & 7;
+        *reinterpret_cast<uint4*>(prow + blk * BM * 128 + ((uu ^ sw) << 4)) = w;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[b2]);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok && n_kv > 0) {
+      ok = mbar_wait(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, abort_flag, p.status, 9);
+      ok = __all_sync(0xffffffff, ok);
+    }
+    if (ok && n_kv > 0) {
+      tc_fence_after();
+      const bool row_ok = qi < L;
+      const float inv_l = 1.0f / l;
+      T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        float o[32];
+        tmem_ld32(lane_base + 256 + c * 32, o);
+        tmem_wait_ld();
+        if (row_ok) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint4 w;
+            w.x = Pk2<T>::pack(o[u * 8 + 0] * inv_l, o[u * 8 + 1] * inv_l);
+            w.y = Pk2<T>::pack(o[u * 8 + 2] * inv_l, o[u * 8 + 3] * inv_l);
+            w.z = Pk2<T>::pack(o[u * 8 + 4] * inv_l, o[u * 8 + 5] * inv_l);
+            w.w = Pk2<T>::pack(o[u * 8 + 6] * inv_l, o[u * 8 + 7] * inv_l);
+            *reinterpret_cast<uint4*>(orow + c * 32 + u * 8) = w;
+          }
+        }
+      }
+      if (row_ok && p.lse != nullptr)
+        p.lse[(seq_start + qi) * p.H + h] = (m_used + log2f(l)) * 0.69314718055994531f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc<512>(tmem);
+  }
+}
+
+template <int D, typename T, bool CAUSAL>
+int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+               const FwdParams& p, int64_t grid, cudaStream_t s) {
+  auto kern = attn_fwd_kernel<D, T, CAUSAL>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    SCREE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        FwdCfg<D>::SMEM));
+    attr_set[dev & 63] = true;
+  }
+  ProfScope prof(PROF_ATTN_FWD, s);
+  kern<<<(unsigned)grid, kThreads, FwdCfg<D>::SMEM, s>>>(tq, tk, tv, p);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+}  // namespace
+}  // namespace scree
+
+using namespace scree;
+
+extern "C" size_t scree_attn_fwd_workspace_size(int64_t B, int64_t T, int64_t H, int D) {
+  (void)H;
+  (void)D;
+  return schedule_bytes(B, T, BM);
+}
+
+extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64_t q_rs,
+                              int64_t q_hs, int64_t k_rs, int64_t k_hs, int64_t v_rs,
+                              int64_t v_hs, const void* offsets, int offs_is_i64, int64_t B,
+                              int64_t T, int64_t H, int D, int dtype, int causal, float scale,
+                              int64_t max_seqlen, void* o, int64_t o_rs, int64_t o_hs, float* lse,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  (void)max_seqlen;
+  SCREE_CHECK_ARG(B >= 1 && T >= 0 && H >= 1, "attn_fwd: bad sizes B=%lld T=%lld H=%lld",
+                  (long long)B, (long long)T, (long long)H);
+  SCREE_CHECK_ARG(T < (1ll << 31) && H < 65536, "attn_fwd: T or H too large");
+  if (D != 32 && D != 64 && D != 128) {
+    set_last_error("attn_fwd: head_dim %d unsupported (32, 64, 128)", D);
+    return SCREE_ERR_UNSUPPORTED;
+  }
+  SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16, "attn_fwd: fp16 or bf16 only");
+  if (T == 0) return SCREE_OK;
+  SCREE_CHECK_ARG(q && k && v && o && offsets, "attn_fwd: null pointer");
+  SCREE_CHECK_ARG(workspace && workspace_bytes >= schedule_bytes(B, T, BM),
+                  "attn_fwd: workspace too small");
+  SCREE_CHECK_ARG(((uintptr_t)o % 16) == 0 && (o_rs % 8) == 0 && (o_hs % 8) == 0,
+                  "attn_fwd: output must be 16-byte aligned with strides multiple of 8");
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool bf16 = dtype == SCREE_BF16;
+  const int swb = D >= 64 ? 128 : 64;
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = make_thd_map(&tq, q, T, H, D, q_rs, q_hs, swb / 2, BM, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tk, k, T, H, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tv, v, T, H, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
+  if ((rc = launch_build_schedule(offsets, offs_is_i64, B, BM, BN, causal, 0, workspace, s)))
+    return rc;
+  FwdParams p;
+  p.offs = offsets;
+  p.is64 = offs_is_i64;
+  p.H = (int)H;
+  p.T = (int)T;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.tile_count = reinterpret_cast<const int32_t*>(workspace);
+  p.status = device_status_ptr();
+  p.tiles = reinterpret_cast<const TileRef*>((const char*)workspace + 16);
+  p.o = o;
+  p.o_rs = o_rs;
+  p.o_hs = o_hs;
+  p.lse = lse;
+  const int64_t grid = max_tiles(B, T, BM) * H;
+  SCREE_CHECK_ARG(grid < (1ll << 31), "attn_fwd: grid too large");
+#define SCREE_FWD_CASE(DD)                                                              \
+  if (D == DD) {                                                                        \
+    if (bf16)                                                                           \
+      return causal ? launch_fwd<DD, __nv_bfloat16, true>(tq, tk, tv, p, grid, s)       \
+                    : launch_fwd<DD, __nv_bfloat16, false>(tq, tk, tv, p, grid, s);     \
+    return causal ? launch_fwd<DD, __half, true>(tq, tk, tv, p, grid, s)                \
+                  : launch_fwd<DD, __half, false>(tq, tk, tv, p, grid, s);              \
+  }
+  SCREE_FWD_CASE(128)
+  SCREE_FWD_CASE(64)
+  SCREE_FWD_CASE(32)
+#undef SCREE_FWD_CASE
+  return SCREE_ERR_UNSUPPORTED;
+}

@@ -1,0 +1,100 @@
+// common.cuh — shared host/device helpers of libscree_b200: status codes, the
+// thread-local last-error message, the device status word, dtype helpers.
+#pragma once
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include "../../include/scree_b200.h"
+
+namespace scree {
+
+// Device status word: 0 = ok, otherwise (code << 16) | site of the first error.
+// It lives in common.cu; kernels receive its address (device_status_ptr()).
+enum : int { SCREE_DEVERR_WAIT_TIMEOUT = 1, SCREE_DEVERR_BAD_INPUT = 2 };
+
+__device__ __forceinline__ void record_device_error(int* status, int code, int site) {
+  if (status) atomicCAS(status, 0, (code << 16) | (site & 0xFFFF));
+}
+
+// Device address of the status word on the current device (looked up once per
+// device with cudaGetSymbolAddress), or nullptr if the lookup failed.
+int* device_status_ptr();
+
+// Host-side error reporting: every C entry point returns a scree_status and
+// leaves a message retrievable through scree_last_error().
+void set_last_error(const char* fmt, ...);
+
+#define SCREE_CHECK_ARG(cond, ...)            \
+  do {                                        \
+    if (!(cond)) {                            \
+      ::scree::set_last_error(__VA_ARGS__);   \
+      return SCREE_ERR_INVALID;               \
+    }                                         \
+  } while (0)
+
+#define SCREE_CUDA_TRY(expr)                                                        \
+  do {                                                                              \
+    cudaError_t _e = (expr);                                                        \
+    if (_e != cudaSuccess) {                                                        \
+      ::scree::set_last_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), \
+                              __FILE__, __LINE__);                                  \
+      return SCREE_ERR_CUDA;                                                        \
+    }                                                                               \
+  } while (0)
+
+// Every kernel launch of the library goes through SCREE_LAUNCH_CHECK, which also
+// counts it (scree_launch_count()).
+void count_launch();
+#define SCREE_LAUNCH_CHECK()            \
+  do {                                  \
+    SCREE_CUDA_TRY(cudaGetLastError()); \
+    ::scree::count_launch();            \
+  } while (0)
+
+// Optional per-kernel timing (scree_profile_enable): CUDA events recorded on the
+// launch stream around the main kernel of an entry point.
+enum ProfKernel : int { PROF_ATTN_FWD = 0, PROF_ATTN_BWD = 1, PROF_NORM_FWD = 2, PROF_NORM_BWD = 3, PROF_N = 4 };
+struct ProfScope {
+  int kernel;
+  cudaStream_t stream;
+  cudaEvent_t start = nullptr;
+  ProfScope(int k, cudaStream_t s);
+  ~ProfScope();
+};
+
+inline size_t dtype_size(int dt) {
+  switch (dt) {
+    case SCREE_F16: return 2;
+    case SCREE_BF16: return 2;
+    case SCREE_F32: return 4;
+    default: return 0;
+  }
+}
+
+int num_sms();  // cached SM count of the current device
+
+// Element <-> float conversion for the three activation dtypes.
+template <typename T> struct Cvt;
+template <> struct Cvt<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+};
+template <> struct Cvt<__half> {
+  static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+  static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
+};
+template <> struct Cvt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+// Offsets may be int32 or int64; read either as int64.
+__device__ __forceinline__ int64_t load_offset(const void* offs, int is_i64, int64_t i) {
+  return is_i64 ? reinterpret_cast<const int64_t*>(offs)[i]
+                : static_cast<int64_t>(reinterpret_cast<const int32_t*>(offs)[i]);
+}
+
+}  // namespace scree

@@ -1,0 +1,261 @@
+// gather.cu — the offset gathers of scree._core on the GPU: pack, to_padded,
+// from_padded.  All are byte copies (bit-exact for every dtype) and HBM-bound:
+// each moves its rows once with 16-byte vector accesses when every row start
+// is 16-byte aligned, else falls back to element-width accesses.  Grids are a
+// multiple of the SM count and grid-stride over the output.
+#include <algorithm>
+#include "common.cuh"
+
+namespace scree {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Largest power-of-two access width (<= 16 bytes) that divides every address
+// the kernel touches.
+int pick_width(int64_t row_bytes, std::initializer_list<uintptr_t> ptrs) {
+  int w = 16;
+  while (w > 1 && (row_bytes % w) != 0) w >>= 1;
+  for (uintptr_t p : ptrs)
+    while (w > 1 && (p % w) != 0) w >>= 1;
+  return w;
+}
+
+template <int W> struct Vec;
+template <> struct Vec<16> { using T = uint4; };
+template <> struct Vec<8> { using T = uint2; };
+template <> struct Vec<4> { using T = uint32_t; };
+template <> struct Vec<2> { using T = uint16_t; };
+template <> struct Vec<1> { using T = uint8_t; };
+
+int grid_for(int64_t work_items) {
+  int64_t per_sm = 8;  // 8 x 256 threads resident per SM
+  int64_t g = (work_items + kThreads - 1) / kThreads;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(g, (int64_t)num_sms() * per_sm));
+}
+
+// Binary search: largest b with offsets[b] <= row, over b in [0, B).
+__device__ __forceinline__ int64_t find_seq(const void* offs, int is64, int64_t B, int64_t row) {
+  int64_t lo = 0, hi = B - 1;
+  while (lo < hi) {
+    int64_t mid = (lo + hi + 1) >> 1;
+    if (load_offset(offs, is64, mid) <= row) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// ---------------------------------------------------------------- pack
+// Output vector v (W bytes) lies in row t = v*W / row_bytes of sequence b; it is
+// copied from src_ptrs[b] at the same byte position relative to the sequence.
+template <int W>
+__global__ void pack_kernel(const void* const* __restrict__ src, const void* offs, int is64,
+                            int64_t B, int64_t row_bytes, int64_t nvec, void* __restrict__ dst) {
+  using V = typename Vec<W>::T;
+  const int64_t vec_per_row = row_bytes / W;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = v / vec_per_row;
+    int64_t b = find_seq(offs, is64, B, row);
+    int64_t rel = v - load_offset(offs, is64, b) * vec_per_row;
+    reinterpret_cast<V*>(dst)[v] = reinterpret_cast<const V*>(src[b])[rel];
+  }
+}
+
+// ---------------------------------------------------------------- to_padded
+template <int W>
+__global__ void to_padded_kernel(const void* __restrict__ values, const void* offs, int is64,
+                                 int64_t B, int64_t max_len, int64_t row_bytes, uint4 fill16,
+                                 int side_left, void* __restrict__ padded,
+                                 uint8_t* __restrict__ mask) {
+  using V = typename Vec<W>::T;
+  const int64_t vec_per_row = row_bytes / W;
+  const int64_t per_seq = max_len * vec_per_row;
+  const int64_t nvec = B * per_seq;
+  V fill;
+  memcpy(&fill, &fill16, sizeof(V));
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (int64_t v = tid; v < nvec; v += stride) {
+    int64_t b = v / per_seq;
+    int64_t j = (v - b * per_seq) / vec_per_row;
+    int64_t inner = v - b * per_seq - j * vec_per_row;
+    int64_t s = load_offset(offs, is64, b), e = load_offset(offs, is64, b + 1);
+    int64_t len = e - s;
+    int64_t src_row = side_left ? j - (max_len - len) : j;
+    V out = fill;
+    if (src_row >= 0 && src_row < len)
+      out = reinterpret_cast<const V*>(values)[(s + src_row) * vec_per_row + inner];
+    reinterpret_cast<V*>(padded)[v] = out;
+  }
+  if (mask != nullptr) {
+    for (int64_t i = tid; i < B * max_len; i += stride) {
+      int64_t b = i / max_len, j = i - b * max_len;
+      int64_t len = load_offset(offs, is64, b + 1) - load_offset(offs, is64, b);
+      mask[i] = side_left ? (j >= max_len - len) : (j < len);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- from_padded
+// Step 1a: one CTA per padded row writes its mask count into offsets[b+1].
+__global__ void padded_count_kernel(const uint8_t* __restrict__ mask, int64_t max_len,
+                                    int32_t* __restrict__ offsets) {
+  __shared__ int red[32];
+  const int64_t b = blockIdx.x;
+  int cnt = 0;
+  for (int64_t j = threadIdx.x; j < max_len; j += blockDim.x) cnt += mask[b * max_len + j] != 0;
+  for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffff, cnt, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = cnt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+    offsets[b + 1] = s;
+    if (b == 0) offsets[0] = 0;
+  }
+}
+
+// Step 1b: single-CTA in-place inclusive scan of offsets[1..B], 1024 at a time.
+__global__ void inplace_scan_kernel(int32_t* __restrict__ offsets, int64_t B) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t base = 0; base < B; base += blockDim.x) {
+    int64_t i = base + threadIdx.x;
+    int32_t v = i < B ? offsets[i + 1] : 0;
+    for (int o = 1; o < 32; o <<= 1) {
+      int32_t n = __shfl_up_sync(0xffffffff, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_sums[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+      int32_t ws = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        int32_t n = __shfl_up_sync(0xffffffff, ws, o);
+        if (lane >= o) ws += n;
+      }
+      warp_sums[lane] = ws;
+    }
+    __syncthreads();
+    int32_t add = carry + (wid > 0 ? warp_sums[wid - 1] : 0);
+    if (i < B) offsets[i + 1] = v + add;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = v + add;
+    __syncthreads();
+  }
+}
+
+template <int W>
+__global__ void from_padded_kernel(const void* __restrict__ padded,
+                                   const int32_t* __restrict__ offs, int64_t B, int64_t max_len,
+                                   int64_t row_bytes, int64_t nvec, void* __restrict__ values) {
+  using V = typename Vec<W>::T;
+  const int64_t vec_per_row = row_bytes / W;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
+       v += (int64_t)gridDim.x * blockDim.x) {
+    int64_t row = v / vec_per_row;
+    int64_t inner = v - row * vec_per_row;
+    int64_t b = find_seq(offs, 0, B, row);
+    int64_t j = row - offs[b];
+    reinterpret_cast<V*>(values)[v] =
+        reinterpret_cast<const V*>(padded)[(b * max_len + j) * vec_per_row + inner];
+  }
+}
+
+}  // namespace
+}  // namespace scree
+
+using namespace scree;
+
+#define DISPATCH_WIDTH(w, KERNEL, GRID, STREAM, ...)                                      \
+  switch (w) {                                                                            \
+    case 16: KERNEL<16><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;                \
+    case 8: KERNEL<8><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;                  \
+    case 4: KERNEL<4><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;                  \
+    case 2: KERNEL<2><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;                  \
+    default: KERNEL<1><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;                 \
+  }
+
+extern "C" int scree_pack(const void* const* src_ptrs, const void* offsets, int offs_is_i64,
+                          int64_t B, int64_t T, int64_t row_bytes, int64_t src_align, void* dst,
+                          void* stream) {
+  SCREE_CHECK_ARG(B >= 1 && T >= 0 && row_bytes >= 0, "scree_pack: bad sizes");
+  if (T == 0 || row_bytes == 0) return SCREE_OK;
+  SCREE_CHECK_ARG(src_ptrs && offsets && dst, "scree_pack: null pointer");
+  SCREE_CHECK_ARG(src_align >= 1, "scree_pack: src_align must be >= 1");
+  // The source pointers live in device memory, so the caller states their
+  // common alignment; the access width divides it, row_bytes and dst.
+  int w = pick_width(row_bytes, {(uintptr_t)dst, (uintptr_t)src_align});
+  int64_t nvec = T * row_bytes / w;
+  cudaStream_t s = (cudaStream_t)stream;
+  DISPATCH_WIDTH(w, pack_kernel, grid_for(nvec), s, src_ptrs, offsets, offs_is_i64, B, row_bytes,
+                 nvec, dst);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+extern "C" int scree_to_padded(const void* values, const void* offsets, int offs_is_i64,
+                               int64_t B, int64_t max_len, int64_t row_bytes, int64_t elem_bytes,
+                               const void* fill_pattern_host, int side_left, void* padded,
+                               uint8_t* mask, void* stream) {
+  SCREE_CHECK_ARG(B >= 0 && max_len >= 0 && row_bytes >= 0, "scree_to_padded: bad sizes");
+  SCREE_CHECK_ARG(elem_bytes == 1 || elem_bytes == 2 || elem_bytes == 4 || elem_bytes == 8,
+                  "scree_to_padded: elem_bytes must be 1, 2, 4 or 8");
+  SCREE_CHECK_ARG(fill_pattern_host != nullptr, "scree_to_padded: null fill pattern");
+  if (B == 0 || max_len == 0) return SCREE_OK;
+  // Build a 16-byte fill vector by repeating the element pattern.
+  uint8_t fill[16];
+  for (int i = 0; i < 16; ++i) fill[i] = ((const uint8_t*)fill_pattern_host)[i % elem_bytes];
+  uint4 fill16;
+  memcpy(&fill16, fill, 16);
+  int w = row_bytes == 0 ? 1 : pick_width(row_bytes, {(uintptr_t)values, (uintptr_t)padded});
+  if (w < elem_bytes && row_bytes > 0) {
+    // The fill vector repeats whole elements only when w is a multiple of elem_bytes.
+    SCREE_CHECK_ARG(false, "scree_to_padded: misaligned buffers for element size %lld",
+                    (long long)elem_bytes);
+  }
+  int64_t nvec = row_bytes == 0 ? 0 : B * max_len * (row_bytes / w);
+  int64_t work = std::max<int64_t>(nvec, B * max_len);
+  cudaStream_t s = (cudaStream_t)stream;
+  DISPATCH_WIDTH(w, to_padded_kernel, grid_for(work), s, values, offsets, offs_is_i64, B,
+                 max_len, row_bytes == 0 ? w : row_bytes, fill16, side_left,
+                 row_bytes == 0 ? nullptr : padded, mask);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+extern "C" int scree_padded_lengths(const uint8_t* mask, int64_t B, int64_t max_len,
+                                    int32_t* offsets_out, void* stream) {
+  SCREE_CHECK_ARG(B >= 1 && max_len >= 0, "scree_padded_lengths: bad sizes");
+  SCREE_CHECK_ARG(offsets_out != nullptr, "scree_padded_lengths: null offsets");
+  SCREE_CHECK_ARG(B < (1ll << 31), "scree_padded_lengths: batch too large");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (max_len == 0) {
+    SCREE_CUDA_TRY(cudaMemsetAsync(offsets_out, 0, (B + 1) * sizeof(int32_t), s));
+    return SCREE_OK;
+  }
+  SCREE_CHECK_ARG(mask != nullptr, "scree_padded_lengths: null mask");
+  padded_count_kernel<<<(unsigned)B, 256, 0, s>>>(mask, max_len, offsets_out);
+  SCREE_LAUNCH_CHECK();
+  inplace_scan_kernel<<<1, 1024, 0, s>>>(offsets_out, B);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+extern "C" int scree_from_padded(const void* padded, const int32_t* offsets, int64_t B,
+                                 int64_t max_len, int64_t T, int64_t row_bytes, void* values,
+                                 void* stream) {
+  SCREE_CHECK_ARG(B >= 1 && T >= 0 && max_len >= 0 && row_bytes >= 0,
+                  "scree_from_padded: bad sizes");
+  if (T == 0 || row_bytes == 0) return SCREE_OK;
+  int w = pick_width(row_bytes, {(uintptr_t)padded, (uintptr_t)values});
+  int64_t nvec = T * row_bytes / w;
+  cudaStream_t s = (cudaStream_t)stream;
+  DISPATCH_WIDTH(w, from_padded_kernel, grid_for(nvec), s, padded, offsets, B, max_len, row_bytes,
+                 nvec, values);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}

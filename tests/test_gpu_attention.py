@@ -1,0 +1,231 @@
+"""Parity of the sm_100a attention kernels with the oracle (GPU only).
+
+Bar: max-abs error <= 2e-3 (fp16) / 1e-2 (bf16) for out, dq, dk, dv relative to
+the fp64 oracle run on the same 16-bit inputs; LSE within 1e-3 (it is fp32).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import decode16, load_golden
+from gpu_helpers import ATTN_TOL, attn_reference, max_err, to64
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(lengths, H, D, dtype, causal, device, seed=0, offs_dtype=torch.int32):
+    from scree_b200 import workloads
+    from scree_b200.kernels.native import varlen_attention_triton, varlen_attention_triton_backward
+
+    q, k, v, do = workloads.make_qkv(lengths, H, D, dtype, device, seed=seed)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=offs_dtype, device=device)
+    out, lse = varlen_attention_triton(q, k, v, cu, causal=causal, return_lse=True)
+    dq, dk, dv = varlen_attention_triton_backward(do, q, k, v, out, lse, cu, causal=causal)
+    torch.cuda.synchronize()
+    return (q, k, v, do), (out, lse, dq, dk, dv)
+
+
+def _check(lengths, H, D, dtype, causal, device, heads=None, seed=0, check_bwd=True, offs_dtype=torch.int32):
+    ins, outs = _run(lengths, H, D, dtype, causal, device, seed, offs_dtype)
+    ref = attn_reference(*ins, lengths, causal, heads)
+    sl = slice(None) if heads is None else heads
+    tol = ATTN_TOL[dtype]
+    names = ("out", "lse", "dq", "dk", "dv")
+    errs = {}
+    for name, got, want in zip(names, outs, ref):
+        if name != "out" and name != "lse" and not check_bwd:
+            continue
+        g = to64(got[:, sl])
+        errs[name] = max_err(g, want)
+    for name, e in errs.items():
+        lim = 1e-3 if name == "lse" else tol
+        assert e <= lim, f"{name}: max abs err {e:.3e} > {lim} ({errs})"
+    from scree_b200 import _lib
+
+    assert _lib.device_status() == 0
+    return errs
+
+
+EDGE_LENGTHS = [
+    [1],
+    [1, 1, 1],
+    [2, 3],
+    [127, 128, 129],
+    [255, 1, 257],
+    [5, 0, 9, 300],
+    [64, 17, 200, 33],
+]
+
+
+@pytest.mark.parametrize("lengths", EDGE_LENGTHS, ids=lambda l: "L" + "_".join(map(str, l)))
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_edge_lengths_bf16(cuda, lengths, D, causal):
+    _check(lengths, 2, D, torch.bfloat16, causal, cuda)
+
+
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_fp16(cuda, D, causal):
+    _check([100, 1, 513, 64], 3, D, torch.float16, causal, cuda, seed=1)
+
+
+def test_attention_int64_offsets(cuda):
+    _check([70, 300, 2], 2, 64, torch.float16, True, cuda, seed=2, offs_dtype=torch.int64)
+
+
+@pytest.mark.parametrize("name", ["attn_d32_f16_c0", "attn_d32_f16_c1", "attn_d128_bf16_c1"])
+def test_attention_golden(cuda, name):
+    """Against the reference's own outputs (fixtures made by running scree)."""
+    from scree_b200.kernels.native import varlen_attention_triton, varlen_attention_triton_backward
+
+    g = load_golden(name)
+    dt = str(g["dtype"])
+    tdt = torch.float16 if dt == "float16" else torch.bfloat16
+    q, k, v, do = (torch.tensor(decode16(g[n], dt), dtype=torch.float32).to(tdt).to(cuda) for n in ("q", "k", "v", "do"))
+    lengths = [int(x) for x in g["lengths"]]
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device=cuda)
+    causal = bool(g["causal"])
+    out, lse = varlen_attention_triton(q, k, v, cu, causal=causal, return_lse=True)
+    dq, dk, dv = varlen_attention_triton_backward(do, q, k, v, out, lse, cu, causal=causal)
+    tol = ATTN_TOL[tdt]
+    for name_, got in (("out", out), ("dq", dq), ("dk", dk), ("dv", dv)):
+        e = max_err(to64(got), g[name_])
+        assert e <= tol, f"{name_}: {e}"
+
+
+def test_attention_cfg2_head_subset(cuda):
+    """cfg2 (16 seqs, 12160 tokens, H16 D64 fp16, causal) checked on 2 heads."""
+    from scree_b200 import workloads
+
+    _check(workloads.cfg2_lengths(), 16, 64, torch.float16, True, cuda, heads=slice(0, 2))
+
+
+def test_attention_cfg4_full_size_sampled(cuda):
+    """cfg4 at full size (T=158330, H32, D128 bf16, causal): the kernels run on the
+    whole batch; the oracle checks the shortest, a median and the longest
+    sequence on heads 0 and 31.  Known answer: each sequence's first output row
+    equals its first V row."""
+    from scree_b200 import workloads
+    from scree_b200.kernels.native import varlen_attention_triton, varlen_attention_triton_backward
+
+    lengths = workloads.cfg4_lengths()
+    H, D = 32, 128
+    q, k, v, do = workloads.make_qkv(lengths, H, D, "bfloat16", cuda, seed=0)
+    offs = np.concatenate([[0], np.cumsum(lengths)])
+    cu = torch.tensor(offs, dtype=torch.int32, device=cuda)
+    out, lse = varlen_attention_triton(q, k, v, cu, causal=True, return_lse=True)
+    dq, dk, dv = varlen_attention_triton_backward(do, q, k, v, out, lse, cu, causal=True)
+    torch.cuda.synchronize()
+    for t in (out, lse, dq, dk, dv):
+        assert torch.isfinite(t).all()
+    first = torch.tensor(offs[:-1], device=cuda, dtype=torch.long)
+    assert torch.equal(out[first], v[first])
+    order = np.argsort(lengths)
+    picks = [int(order[0]), int(order[len(order) // 2]), int(order[-1])]
+    for b in picks:
+        s, e = int(offs[b]), int(offs[b + 1])
+        for h in (0, H - 1):
+            sub = [t[s:e, h : h + 1] for t in (q, k, v, do)]
+            ref = attn_reference(*sub, [e - s], True)
+            got = [t[s:e, h : h + 1] for t in (out, lse, dq, dk, dv)]
+            for name, gt, rf in zip(("out", "lse", "dq", "dk", "dv"), got, ref):
+                lim = 1e-3 if name == "lse" else 1e-2
+                err = max_err(to64(gt), rf)
+                assert err <= lim, f"seq {b} (L={e-s}) head {h} {name}: {err}"
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_attention_cfg5_skew_forward(cuda, causal):
+    """cfg5 (lengths lognormal sigma 1.2, four length-1 sequences, H16 D128 bf16):
+    forward only, as configured; shortest / longest sequences checked on head 0."""
+    from scree_b200 import workloads
+    from scree_b200.kernels.native import varlen_attention_triton
+
+    lengths = workloads.cfg5_lengths()
+    q, k, v = workloads.make_qkv(lengths, 16, 128, "bfloat16", cuda, seed=0, with_do=False)
+    offs = np.concatenate([[0], np.cumsum(lengths)])
+    cu = torch.tensor(offs, dtype=torch.int32, device=cuda)
+    out, lse = varlen_attention_triton(q, k, v, cu, causal=causal, return_lse=True)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all() and torch.isfinite(lse).all()
+    for b in (0, int(np.argmax(lengths))):
+        s, e = int(offs[b]), int(offs[b + 1])
+        qn, kn, vn = (to64(t[s:e, 0:1]) for t in (q, k, v))
+        ro, rl = oracle.attention_fwd(qn, kn, vn, [0, e - s], causal=causal)
+        assert max_err(to64(out[s:e, 0:1]), ro) <= 1e-2
+        assert max_err(to64(lse[s:e, 0:1]), rl) <= 1e-3
+
+
+def test_attention_strided_inputs_and_out_buffers(cuda):
+    """q/k/v as views of a fused (T, 3, H, D) buffer (strided rows), caller-given
+    out and lse buffers."""
+    from scree_b200.kernels.native import varlen_attention_triton
+
+    lengths = [33, 150]
+    T, H, D = sum(lengths), 2, 64
+    g = torch.Generator().manual_seed(5)
+    qkv = torch.randn((T, 3, H, D), generator=g).to(torch.bfloat16).to(cuda)
+    q, k, v = qkv[:, 0], qkv[:, 1], qkv[:, 2]
+    cu = torch.tensor([0, 33, 183], dtype=torch.int32, device=cuda)
+    out = torch.empty((T, H, D), dtype=torch.bfloat16, device=cuda)
+    lse = torch.empty((T, H), dtype=torch.float32, device=cuda)
+    o2, l2 = varlen_attention_triton(q, k, v, cu, causal=True, return_lse=True, out=out, lse_buffer=lse)
+    assert o2 is out and l2 is lse
+    ro, rl = oracle.attention_fwd(to64(q), to64(k), to64(v), [0, 33, 183], causal=True)
+    assert max_err(to64(out), ro) <= 1e-2
+    assert max_err(to64(lse), rl) <= 1e-3
+
+
+def test_attention_autograd_matches_backward(cuda):
+    from scree_b200 import workloads
+    from scree_b200.kernels.native import varlen_attention_triton_autograd
+
+    lengths = [40, 200, 1]
+    q, k, v, do = workloads.make_qkv(lengths, 2, 128, "float16", cuda, seed=3)
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    cu = torch.tensor([0, 40, 240, 241], dtype=torch.int32, device=cuda)
+    out = varlen_attention_triton_autograd(q, k, v, cu, causal=True)
+    out.backward(do)
+    ref = attn_reference(q, k, v, do, lengths, True)
+    for got, want in zip((out, q.grad, k.grad, v.grad), (ref[0], ref[2], ref[3], ref[4])):
+        assert max_err(to64(got), want) <= 2e-3
+
+
+def test_array_level_attention(cuda):
+    """scree_b200.kernels.varlen_attention over packed Arrays (reference/varlen_attention.py:10)."""
+    import scree_b200 as scree
+    from scree_b200.kernels import varlen_attention
+
+    g = torch.Generator().manual_seed(0)
+    lens = [3, 5, 2]
+    mk = lambda: [torch.randn((n, 2, 32), generator=g).to(torch.float16).to(cuda) for n in lens]  # noqa: E731
+    qs, ks, vs = mk(), mk(), mk()
+    q, k, v = scree.pack(qs), scree.pack(ks), scree.pack(vs)
+    out = varlen_attention(q, k, v, causal=True)
+    assert out.offsets is q.offsets
+    rows = scree.unpack(out)
+    for i in range(3):
+        torch.testing.assert_close(rows[i][0], vs[i][0], atol=1e-3, rtol=0)
+    k_bad = scree.pack([torch.randn((n, 2, 32)).half().to(cuda) for n in [4, 4, 2]])
+    with pytest.raises(ValueError, match="identical offsets"):
+        varlen_attention(q, k_bad, v)
+
+
+def test_attention_argument_errors(cuda):
+    from scree_b200.kernels.native import varlen_attention_triton
+
+    q = torch.zeros((4, 1, 64), dtype=torch.float32, device=cuda)
+    cu = torch.tensor([0, 4], dtype=torch.int32, device=cuda)
+    with pytest.raises(AssertionError):
+        varlen_attention_triton(q, q, q, cu)
+    q16 = torch.zeros((4, 1, 96), dtype=torch.float16, device=cuda)
+    with pytest.raises(NotImplementedError):
+        varlen_attention_triton(q16, q16, q16, cu)
+    with pytest.raises(AssertionError):
+        varlen_attention_triton(q16.cpu(), q16.cpu(), q16.cpu(), cu.cpu())
