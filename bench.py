@@ -255,12 +255,15 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--max-seqs", type=int, default=0, help="keep only the first N sequences (small profiling case)")
     args = ap.parse_args()
 
     from scree_b200 import workloads
 
     cfg = workloads.attn_config(args.config)
     lengths = list(cfg.lengths)
+    if args.max_seqs:
+        lengths = lengths[: args.max_seqs]
     H, D, causal = cfg.heads, cfg.head_dim, cfg.causal
 
     if args.impl == "reference":

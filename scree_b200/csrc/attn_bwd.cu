@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int qmax = min(BQ, L - q0);
         float* base = p.dq_acc + ((row0 + q0) * p.H + h) * D + ln;
         const int64_t rstride = (int64_t)p.H * D;
-#pragma unroll 8
+#pragma unroll
         for (int c = 0; c < BQ; ++c)
           if (c < qmax) atomicAdd(base + c * rstride, v[c] * sc);
       } else {
@@ -664,6 +664,7 @@ extern "C" int scree_attn_bwd(const void* dout, const void* q, const void* k, co
   const void* ptrs[8] = {dout, q, k, v, o, dq, dk, dv};
   for (const void* ptr : ptrs)
     SCREE_CHECK_ARG(((uintptr_t)ptr % 16) == 0, "attn_bwd: tensors must be 16-byte aligned");
+  SCREE_BIND_DEVICE(stream, q);
   cudaStream_t s = (cudaStream_t)stream;
   char* ws = reinterpret_cast<char*>(workspace);
   if (dtype == SCREE_BF16)

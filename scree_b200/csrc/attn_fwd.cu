@@ -414,6 +414,7 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
                   "attn_fwd: workspace too small");
   SCREE_CHECK_ARG(((uintptr_t)o % 16) == 0 && (o_rs % 8) == 0 && (o_hs % 8) == 0,
                   "attn_fwd: output must be 16-byte aligned with strides multiple of 8");
+  SCREE_BIND_DEVICE(stream, q);
   cudaStream_t s = (cudaStream_t)stream;
   const bool bf16 = dtype == SCREE_BF16;
   const int swb = D >= 64 ? 128 : 64;

@@ -55,6 +55,19 @@ ProfScope::~ProfScope() {
   g_prof_events[kernel].emplace_back(start, stop);
 }
 
+int bind_device(cudaStream_t stream, const void* ptr) {
+  int dev = -1;
+  if (stream != nullptr && stream != cudaStreamLegacy && stream != cudaStreamPerThread) {
+    SCREE_CUDA_TRY(cudaStreamGetDevice(stream, &dev));
+  } else if (ptr != nullptr) {
+    cudaPointerAttributes a;
+    SCREE_CUDA_TRY(cudaPointerGetAttributes(&a, ptr));
+    dev = a.device;
+  }
+  if (dev >= 0) SCREE_CUDA_TRY(cudaSetDevice(dev));
+  return SCREE_OK;
+}
+
 int num_sms() {
   static int cache[64] = {0};
   int dev = 0;

@@ -76,6 +76,16 @@ inline size_t dtype_size(int dt) {
 
 int num_sms();  // cached SM count of the current device
 
+// Makes the device that owns `stream` (or, for the legacy default stream, the
+// memory `ptr` points to) current on the calling thread.  Callers such as
+// torch's autograd worker threads may enter with no CUDA context bound.
+int bind_device(cudaStream_t stream, const void* ptr);
+#define SCREE_BIND_DEVICE(stream, ptr)                          \
+  do {                                                          \
+    int _rc = ::scree::bind_device((cudaStream_t)(stream), ptr); \
+    if (_rc != SCREE_OK) return _rc;                            \
+  } while (0)
+
 // Element <-> float conversion for the three activation dtypes.
 template <typename T> struct Cvt;
 template <> struct Cvt<float> {

@@ -190,6 +190,7 @@ extern "C" int scree_pack(const void* const* src_ptrs, const void* offsets, int 
   // common alignment; the access width divides it, row_bytes and dst.
   int w = pick_width(row_bytes, {(uintptr_t)dst, (uintptr_t)src_align});
   int64_t nvec = T * row_bytes / w;
+  SCREE_BIND_DEVICE(stream, dst);
   cudaStream_t s = (cudaStream_t)stream;
   DISPATCH_WIDTH(w, pack_kernel, grid_for(nvec), s, src_ptrs, offsets, offs_is_i64, B, row_bytes,
                  nvec, dst);
@@ -219,6 +220,7 @@ extern "C" int scree_to_padded(const void* values, const void* offsets, int offs
   }
   int64_t nvec = row_bytes == 0 ? 0 : B * max_len * (row_bytes / w);
   int64_t work = std::max<int64_t>(nvec, B * max_len);
+  SCREE_BIND_DEVICE(stream, mask ? (const void*)mask : padded);
   cudaStream_t s = (cudaStream_t)stream;
   DISPATCH_WIDTH(w, to_padded_kernel, grid_for(work), s, values, offsets, offs_is_i64, B,
                  max_len, row_bytes == 0 ? w : row_bytes, fill16, side_left,
@@ -232,6 +234,7 @@ extern "C" int scree_padded_lengths(const uint8_t* mask, int64_t B, int64_t max_
   SCREE_CHECK_ARG(B >= 1 && max_len >= 0, "scree_padded_lengths: bad sizes");
   SCREE_CHECK_ARG(offsets_out != nullptr, "scree_padded_lengths: null offsets");
   SCREE_CHECK_ARG(B < (1ll << 31), "scree_padded_lengths: batch too large");
+  SCREE_BIND_DEVICE(stream, offsets_out);
   cudaStream_t s = (cudaStream_t)stream;
   if (max_len == 0) {
     SCREE_CUDA_TRY(cudaMemsetAsync(offsets_out, 0, (B + 1) * sizeof(int32_t), s));
@@ -253,6 +256,7 @@ extern "C" int scree_from_padded(const void* padded, const int32_t* offsets, int
   if (T == 0 || row_bytes == 0) return SCREE_OK;
   int w = pick_width(row_bytes, {(uintptr_t)padded, (uintptr_t)values});
   int64_t nvec = T * row_bytes / w;
+  SCREE_BIND_DEVICE(stream, values);
   cudaStream_t s = (cudaStream_t)stream;
   DISPATCH_WIDTH(w, from_padded_kernel, grid_for(nvec), s, padded, offsets, B, max_len, row_bytes,
                  nvec, values);

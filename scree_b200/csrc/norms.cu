@@ -366,6 +366,7 @@ int norm_fwd(const void* x, int64_t xs, const void* w, const void* b, int w_dtyp
     return SCREE_ERR_UNSUPPORTED;
   }
   if (!w) w_dtype = dtype;
+  SCREE_BIND_DEVICE(stream, x);
   cudaStream_t s = (cudaStream_t)stream;
   return dispatch_types<LAYER>(dtype, w_dtype, [&](auto* tp, auto* wp) {
     using T = std::remove_pointer_t<decltype(tp)>;
@@ -389,6 +390,7 @@ int norm_bwd(const void* dy, const void* x, const void* w, int w_dtype, const fl
   SCREE_CHECK_ARG(!LAYER || mean, "layernorm bwd: mean required");
   const int es = (int)dtype_size(dtype);
   SCREE_CHECK_ARG(es > 0, "norm bwd: bad dtype %d", dtype);
+  SCREE_BIND_DEVICE(stream, x);
   cudaStream_t s = (cudaStream_t)stream;
   const bool want_w = dw != nullptr, want_b = LAYER && db != nullptr;
   if (rows == 0) {

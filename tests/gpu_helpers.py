@@ -5,9 +5,21 @@ import torch
 
 import oracle
 
-# Attention tolerance (max abs vs the fp64 oracle on the same 16-bit inputs):
-# 2e-3 for fp16, 1e-2 for bf16, as the north-star parity bar states.
+# Attention tolerance vs the fp64 oracle on the same 16-bit inputs: max abs
+# 2e-3 for fp16, 1e-2 for bf16 (the north-star parity bar), plus the rounding
+# of the result to its 16-bit storage type (half an ulp: 2^-12 relative for
+# fp16, 2^-9 for bf16; a flat 1e-2 is finer than bf16 can represent once |x| >= 4).
 ATTN_TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+ATTN_REL = {torch.float16: 2.0**-11, torch.bfloat16: 2.0**-8}
+
+
+def excess(got, want, atol, rtol):
+    """Largest |got - want| - (atol + rtol |want|); <= 0 means within bounds."""
+    g = np.asarray(got, dtype=np.float64)
+    w = np.asarray(want, dtype=np.float64)
+    if g.size == 0:
+        return -atol
+    return float(np.max(np.abs(g - w) - (atol + rtol * np.abs(w))))
 
 
 def to64(t):
