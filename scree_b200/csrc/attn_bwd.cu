@@ -49,7 +49,9 @@ struct BwdCfg {
   static constexpr int OFF_PT = OFF_DO + STAGES * QT_BYTES;
   static constexpr int OFF_DS = OFF_PT + PT_BYTES;
   static constexpr int OFF_LD = OFF_DS + PT_BYTES;          // lse2 / delta [2][2][BQ] fp32
-  static constexpr int OFF_BAR = OFF_LD + 2 * 2 * BQ * 4;
+  static constexpr int OFF_DQ = OFF_LD + 2 * 2 * BQ * 4;    // DQT: dQ tile [BQ][D] fp32
+  static constexpr int DQ_BYTES = DQT ? BQ * D * 4 : 0;
+  static constexpr int OFF_BAR = OFF_DQ + DQ_BYTES;
   // At least 120 KB so two CTAs (each holding all 512 TMEM columns) never share an SM.
   static constexpr int SMEM_RAW = OFF_BAR + 512 + 1024;
   static constexpr int SMEM = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
@@ -66,8 +68,8 @@ struct BwdParams {
   int T;
   float scale;       // softmax scale
   float scale_log2;  // scale * log2(e)
-  const int32_t* tile_count;
-  const TileRef* tiles;
+  const void* sched;  // schedule (attn_common.cuh)
+  int64_t B;
   int* status;  // device status word
   const float* lse2T;   // [H][T], lse * log2(e)
   const float* deltaT;  // [H][T]
@@ -120,9 +122,12 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-// Named barrier over the 128 threads of warps 0-3.
+// Named barriers over the 128 threads of warps 0-3 and of warps 4-7.
 __device__ __forceinline__ void softmax_group_sync() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+__device__ __forceinline__ void dq_group_sync() {
+  asm volatile("bar.sync 2, 128;" ::: "memory");
 }
 
 // Row-major [BN][BQ] 16-bit tile in 128B swizzle: write the BQ values of row kr.
@@ -146,7 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
-                    const __grid_constant__ CUtensorMap tm_do, const BwdParams p) {
+                    const __grid_constant__ CUtensorMap tm_do,
+                    const __grid_constant__ CUtensorMap tm_dq, const BwdParams p) {
   using C = BwdCfg<D>;
   constexpr int BQ = C::BQ;
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -155,16 +161,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t ID_DQ = C::DQT ? make_idesc_f16(D, BQ, kBF16, true, true)
                                     : make_idesc_f16(BQ, D, kBF16, true, true);
 
-  const int item = blockIdx.x;
-  const int ntiles = *p.tile_count;
-  if (item >= ntiles * p.H) return;
+  const int64_t item = blockIdx.x;
+  if (item >= total_items(p.sched)) return;
   // A CTA of an earlier failed launch (or of this one) set the status word: skip.
   if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
-  const TileRef tr = p.tiles[item / p.H];
-  const int h = item % p.H;
-  const int64_t row0 = load_offset(p.offs, p.is64, tr.seq);
-  const int L = (int)(load_offset(p.offs, p.is64, tr.seq + 1) - row0);
-  const int k0 = tr.tile * BN;
+  const WorkItem wi = decode_item(p.sched, p.B, p.H, item);
+  const int h = wi.head;
+  const int64_t row0 = load_offset(p.offs, p.is64, wi.seq);
+  const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - row0);
+  const int k0 = wi.j * BN;  // causal: the first key tile has the most query tiles
   const int nq = (L + BQ - 1) / BQ;
   const int i_first = CAUSAL ? k0 / BQ : 0;
   const int n_it = nq - i_first;  // >= 1 since k0 < L
@@ -332,22 +337,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float* lse_h = p.lse2T + (int64_t)h * p.T + row0;
     const float* del_h = p.deltaT + (int64_t)h * p.T + row0;
     bool ok = true;
+    // LSE / Delta of query tile `it` (queries past L read as 0; masked below).
+    // Thread kr fetches entry kr of the 2*BQ values; they are loaded one tile
+    // ahead so the global latency overlaps the current tile's work.
+    auto fetch = [&](int it_, float& a, float& b) {
+      const int q0_ = (i_first + it_) * BQ;
+      if (BQ == 64) {
+        const int q = q0_ + (kr & 63);
+        a = q < L ? (kr < 64 ? lse_h[q] : del_h[q]) : 0.f;
+      } else {
+        const int q = q0_ + kr;
+        a = q < L ? lse_h[q] : 0.f;
+        b = q < L ? del_h[q] : 0.f;
+      }
+    };
+    float pre_a = 0.f, pre_b = 0.f;
+    fetch(0, pre_a, pre_b);
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (i_first + it) * BQ;
       float* lse_s = lds + (it & 1) * 2 * BQ;
       float* del_s = lse_s + BQ;
-      // Stage this tile's LSE and Delta (queries past L read as 0; masked below).
-      if (kr < BQ) {
-        const int q = q0 + kr;
-        lse_s[kr] = q < L ? lse_h[q] : 0.f;
+      if (BQ == 64) {
+        lds[(it & 1) * 2 * BQ + kr] = pre_a;  // [0,64) lse, [64,128) delta
       } else {
-        const int q = q0 + kr - BQ;
-        if (kr - BQ < BQ) del_s[kr - BQ] = q < L ? del_h[q] : 0.f;
+        lse_s[kr] = pre_a;
+        del_s[kr] = pre_b;
       }
-      if (BQ == 128) {  // 128 threads, 2 x 128 values: second half
-        const int q = q0 + kr;
-        del_s[kr] = q < L ? del_h[q] : 0.f;
-      }
+      if (it + 1 < n_it) fetch(it + 1, pre_a, pre_b);
       softmax_group_sync();
       const bool need_mask = (q0 + BQ > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
       // ---- P^T row from S^T
@@ -449,12 +465,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(dq_empty);
-        const int qmax = min(BQ, L - q0);
-        float* base = p.dq_acc + ((row0 + q0) * p.H + h) * D + ln;
-        const int64_t rstride = (int64_t)p.H * D;
+        // Stage the scaled dQ tile as [BQ][D] fp32 and add it into dq_acc with one
+        // TMA reduce.  Queries >= L carry exact zeros (their dS is 0), so adding
+        // the whole box is safe even where it overlaps the next sequence.
+        if (ln == 0 && it > 0) bulk_wait_read_all();
+        dq_group_sync();
+        float* sdq = reinterpret_cast<float*>(smem + C::OFF_DQ);
 #pragma unroll
-        for (int c = 0; c < BQ; ++c)
-          if (c < qmax) atomicAdd(base + c * rstride, v[c] * sc);
+        for (int c = 0; c < BQ; ++c) sdq[c * D + ln] = v[c] * sc;
+        fence_proxy_async_smem();
+        dq_group_sync();
+        if (ln == 0) {
+          tma_reduce_add_3d(&tm_dq, sdq, 0, h, (int)(row0 + q0));
+          bulk_commit();
+        }
       } else {
         const int q = q0 + ln;
         float* base = p.dq_acc + ((row0 + q) * p.H + h) * D;
@@ -474,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(dq_empty);
       }
     }
+    if (C::DQT && ln == 0) bulk_wait_all();  // smem must outlive the reduces
   }
 
   __syncwarp();
@@ -536,7 +561,8 @@ __global__ void cast_dq_kernel(const float* __restrict__ acc, T* __restrict__ dq
 
 template <int D, typename T, bool CAUSAL>
 int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-               const CUtensorMap& tdo, const BwdParams& p, int64_t grid, cudaStream_t s) {
+               const CUtensorMap& tdo, const CUtensorMap& tdq, const BwdParams& p, int64_t grid,
+               cudaStream_t s) {
   auto kern = attn_bwd_kernel<D, T, CAUSAL>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -547,7 +573,7 @@ int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
     attr_set[dev & 63] = true;
   }
   ProfScope prof(PROF_ATTN_BWD, s);
-  kern<<<(unsigned)grid, kThreads, BwdCfg<D>::SMEM, s>>>(tq, tk, tv, tdo, p);
+  kern<<<(unsigned)grid, kThreads, BwdCfg<D>::SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
@@ -562,7 +588,7 @@ BwdWs bwd_ws_layout(int64_t B, int64_t T, int64_t H, int D) {
   w.off_delta = align256(w.off_dq + (size_t)T * H * D * 4);
   w.off_lse2 = align256(w.off_delta + (size_t)T * H * 4);
   w.off_sched = align256(w.off_lse2 + (size_t)T * H * 4);
-  w.total = w.off_sched + schedule_bytes(B, T, BN);
+  w.total = w.off_sched + schedule_bytes(B);
   return w;
 }
 
@@ -583,6 +609,8 @@ int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v,
   if ((rc = make_thd_map(&tv, v, Tn, H, D, rs, hs, swb / 2, BN, swb, bf16))) return rc;
 
   float* dq_acc = reinterpret_cast<float*>(ws + L.off_dq);
+  CUtensorMap tdq;
+  if ((rc = make_thd_map_f32(&tdq, dq_acc, Tn, H, D, bq))) return rc;
   float* deltaT = reinterpret_cast<float*>(ws + L.off_delta);
   float* lse2T = reinterpret_cast<float*>(ws + L.off_lse2);
   void* sched = ws + L.off_sched;
@@ -595,7 +623,7 @@ int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v,
     else bwd_preprocess_kernel<T, 32><<<blocks, 256, 0, s>>>((const T*)o, (const T*)dout, lse, Tn, (int)H, deltaT, lse2T);
     SCREE_LAUNCH_CHECK();
   }
-  if ((rc = launch_build_schedule(offsets, is64, B, BN, bq, causal, 1, sched, s))) return rc;
+  if ((rc = launch_build_schedule(offsets, is64, B, BN, (int)H, sched, s))) return rc;
   BwdParams p;
   p.offs = offsets;
   p.is64 = is64;
@@ -603,9 +631,9 @@ int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v,
   p.T = (int)Tn;
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.tile_count = reinterpret_cast<const int32_t*>(sched);
+  p.sched = sched;
+  p.B = B;
   p.status = device_status_ptr();
-  p.tiles = reinterpret_cast<const TileRef*>((const char*)sched + 16);
   p.lse2T = lse2T;
   p.deltaT = deltaT;
   p.dq_acc = dq_acc;
@@ -618,8 +646,8 @@ int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v,
   }
 #define SCREE_BWD_CASE(DD)                                                        \
   if (D == DD) {                                                                  \
-    rc = causal ? launch_bwd<DD, T, true>(tq, tk, tv, tdo, p, grid, s)            \
-                : launch_bwd<DD, T, false>(tq, tk, tv, tdo, p, grid, s);          \
+    rc = causal ? launch_bwd<DD, T, true>(tq, tk, tv, tdo, tdq, p, grid, s)       \
+                : launch_bwd<DD, T, false>(tq, tk, tv, tdo, tdq, p, grid, s);     \
   }
   SCREE_BWD_CASE(128)
   SCREE_BWD_CASE(64)

@@ -1,78 +1,93 @@
-// attn_common.cu — host side of the attention helpers (tensor-map creation).
+// attn_common.cu — the attention work scheduler and tensor-map creation.
 #include "attn_common.cuh"
 
 namespace scree {
 
-constexpr int kCostBuckets = 4096;
-
-// Per-tile cost in units of inner tiles.
-//   forward  (outer = query tile of `outer` rows, inner = key tiles of `inner`):
-//     causal: key tiles up to the diagonal; non-causal: all key tiles.
-//   backward (outer = key tile, inner = query tiles):
-//     causal: query tiles from the diagonal on; non-causal: all query tiles.
-__device__ __forceinline__ int tile_cost(int64_t L, int t, int outer, int inner, int causal,
-                                         int bwd) {
-  const int64_t n_inner = (L + inner - 1) / inner;
-  if (!causal) return (int)n_inner;
-  if (!bwd) {
-    int64_t last = ((int64_t)(t + 1) * outer - 1) / inner + 1;
-    return (int)(last < n_inner ? last : n_inner);
+// One CTA of 1024 threads.  Sorts (length, index) keys descending with a
+// shared-memory bitonic sort (B <= kSortMax), then an exclusive scan of
+// ntiles * H gives each sequence's first work item.
+__global__ void build_schedule_kernel(const void* offs, int is64, int64_t B, int outer, int H,
+                                      int64_t* total_out, SeqRef* refs) {
+  __shared__ unsigned long long keys[kSortMax];
+  __shared__ long long warp_tot[32];
+  __shared__ long long carry;
+  const bool sorted = B <= kSortMax;
+  int n2 = 1;
+  while (n2 < B) n2 <<= 1;
+  if (sorted) {
+    for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+      unsigned long long key = 0;  // padding sorts last (length 0, index max)
+      if (i < B) {
+        const int64_t L = load_offset(offs, is64, i + 1) - load_offset(offs, is64, i);
+        // descending length, ties by ascending index: key = (L << 32) | ~index
+        key = ((unsigned long long)(L & 0xFFFFFFFF) << 32) | (0xFFFFFFFFu - (unsigned)i);
+      }
+      keys[i] = key;
+    }
+    __syncthreads();
+    for (int k = 2; k <= n2; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+          const int ixj = i ^ j;
+          if (ixj > i) {
+            const bool desc = (i & k) == 0;  // overall descending
+            const unsigned long long a = keys[i], b = keys[ixj];
+            if (desc ? (a < b) : (a > b)) {
+              keys[i] = b;
+              keys[ixj] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
   }
-  int64_t first = ((int64_t)t * outer) / inner;
-  return (int)(n_inner - first);
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  for (int64_t base = 0; base < B; base += blockDim.x) {
+    const int64_t i = base + threadIdx.x;
+    long long items = 0;
+    int32_t seq = 0, nt = 0;
+    if (i < B) {
+      seq = sorted ? (int32_t)(0xFFFFFFFFu - (unsigned)(keys[i] & 0xFFFFFFFFull)) : (int32_t)i;
+      const int64_t L = load_offset(offs, is64, seq + 1) - load_offset(offs, is64, seq);
+      nt = (int32_t)((L + outer - 1) / outer);
+      items = (long long)nt * H;
+    }
+    long long v = items;  // inclusive warp scan
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long n = __shfl_up_sync(0xffffffff, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) warp_tot[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+      long long w = lane < (int)(blockDim.x >> 5) ? warp_tot[lane] : 0;
+      for (int o = 1; o < 32; o <<= 1) {
+        const long long n = __shfl_up_sync(0xffffffff, w, o);
+        if (lane >= o) w += n;
+      }
+      warp_tot[lane] = w;
+    }
+    __syncthreads();
+    const long long incl = carry + (wid > 0 ? warp_tot[wid - 1] : 0) + v;
+    if (i < B) refs[i] = SeqRef{seq, nt, (int64_t)(incl - items)};
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *total_out = carry;
 }
 
-// Builds the tile list sorted by descending cost (counting sort over cost
-// buckets; ties in any order).  One CTA of 1024 threads.  Heavy tiles first
-// lets the hardware block scheduler approximate longest-processing-time-first.
-__global__ void build_schedule_kernel(const void* offs, int is64, int64_t B, int outer, int inner,
-                                      int causal, int bwd, int32_t* count_out,
-                                      TileRef* list) {
-  __shared__ int hist[kCostBuckets];
-  for (int i = threadIdx.x; i < kCostBuckets; i += blockDim.x) hist[i] = 0;
-  __syncthreads();
-  for (int64_t b = threadIdx.x; b < B; b += blockDim.x) {
-    const int64_t L = load_offset(offs, is64, b + 1) - load_offset(offs, is64, b);
-    const int64_t nt = (L + outer - 1) / outer;
-    for (int64_t t = 0; t < nt; ++t) {
-      int c = tile_cost(L, (int)t, outer, inner, causal, bwd);
-      c = c < kCostBuckets - 1 ? c : kCostBuckets - 1;
-      atomicAdd(&hist[c], 1);
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    // Exclusive scan from the most expensive bucket down.
-    int acc = 0;
-    for (int c = kCostBuckets - 1; c >= 0; --c) {
-      int n = hist[c];
-      hist[c] = acc;
-      acc += n;
-    }
-    *count_out = acc;
-  }
-  __syncthreads();
-  for (int64_t b = threadIdx.x; b < B; b += blockDim.x) {
-    const int64_t L = load_offset(offs, is64, b + 1) - load_offset(offs, is64, b);
-    const int64_t nt = (L + outer - 1) / outer;
-    for (int64_t t = 0; t < nt; ++t) {
-      int c = tile_cost(L, (int)t, outer, inner, causal, bwd);
-      c = c < kCostBuckets - 1 ? c : kCostBuckets - 1;
-      int pos = atomicAdd(&hist[c], 1);
-      list[pos] = TileRef{(int32_t)b, (int32_t)t};
-    }
-  }
-}
-
-int launch_build_schedule(const void* offs, int is64, int64_t B, int outer, int inner, int causal,
-                          int bwd, void* ws, cudaStream_t stream) {
-  build_schedule_kernel<<<1, 1024, 0, stream>>>(offs, is64, B, outer, inner, causal, bwd,
-                                                reinterpret_cast<int32_t*>(ws),
-                                                reinterpret_cast<TileRef*>((char*)ws + 16));
+int launch_build_schedule(const void* offs, int is64, int64_t B, int outer, int H, void* ws,
+                          cudaStream_t stream) {
+  build_schedule_kernel<<<1, 1024, 0, stream>>>(offs, is64, B, outer, H,
+                                                reinterpret_cast<int64_t*>(ws),
+                                                reinterpret_cast<SeqRef*>((char*)ws + 16));
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
-
 
 EncodeTiledFn get_encode_tiled() {
   static EncodeTiledFn fn = nullptr;
@@ -114,6 +129,28 @@ int make_thd_map(CUtensorMap* map, const void* base, int64_t T, int64_t H, int D
     set_last_error("cuTensorMapEncodeTiled failed (CUresult %d): T=%lld H=%lld D=%d strides=%lld,%lld",
                    (int)r, (long long)T, (long long)H, D, (long long)row_stride,
                    (long long)head_stride);
+    return SCREE_ERR_CUDA;
+  }
+  return SCREE_OK;
+}
+
+int make_thd_map_f32(CUtensorMap* map, const void* base, int64_t T, int64_t H, int D,
+                     int box_rows) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) {
+    set_last_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return SCREE_ERR_CUDA;
+  }
+  SCREE_CHECK_ARG(((uintptr_t)base % 16) == 0, "fp32 map: base must be 16-byte aligned");
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)D * 4, (cuuint64_t)(H * D * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)D, 1u, (cuuint32_t)box_rows};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled (fp32) failed (CUresult %d)", (int)r);
     return SCREE_ERR_CUDA;
   }
   return SCREE_OK;

@@ -9,28 +9,59 @@
 
 namespace scree {
 
-// A work tile: sequence index and tile index along the outer loop dimension
-// (query tiles in the forward, key tiles in the backward).
-struct TileRef {
-  int32_t seq;
-  int32_t tile;
+// Work schedule.  Work items are (sequence, head, tile) triples enumerated so
+// that the CTAs resident at any moment share data in L2:
+//   sequences in descending length (cost ~ L^2; longest first = LPT order),
+//   then head-major within a sequence, then the sequence's tiles, heaviest first
+//   (forward causal: the last query tile; backward causal: the first key tile).
+// A block index maps to its item by a binary search over SeqRef::item_start.
+struct SeqRef {
+  int32_t seq;         // index into offsets
+  int32_t ntiles;      // tiles of `outer` rows in this sequence
+  int64_t item_start;  // first work item of this sequence (items = ntiles * H)
 };
 
 // Upper bound on the number of tiles of size `rows` over a batch of B
 // sequences with T tokens in total: sum_b ceil(L_b / rows) <= T / rows + B.
 inline int64_t max_tiles(int64_t B, int64_t T, int rows) { return (T + rows - 1) / rows + B; }
 
-// Schedule workspace: [count (int32, padded to 16 B)] [TileRef x max_tiles].
-inline size_t schedule_bytes(int64_t B, int64_t T, int rows) {
-  return 16 + sizeof(TileRef) * (size_t)max_tiles(B, T, rows);
-}
+// Schedule workspace: [total items (int64, padded to 16 B)] [SeqRef x B].
+inline size_t schedule_bytes(int64_t B) { return 16 + sizeof(SeqRef) * (size_t)B; }
 
-// Enqueues the schedule build: writes the tile count and the list of TileRef
-// sorted by descending cost into `ws` (schedule_bytes() bytes).
-//   forward  (outer = query tiles of `outer` rows, inner = key tiles of `inner`)
-//   backward (outer = key tiles, inner = query tiles; bwd = 1)
-int launch_build_schedule(const void* offs, int is64, int64_t B, int outer, int inner, int causal,
-                          int bwd, void* ws, cudaStream_t stream);
+// Sequences sorted by length on the device (one CTA) when B <= kSortMax;
+// larger batches keep their natural order (head-major grouping still applies).
+constexpr int kSortMax = 4096;
+
+int launch_build_schedule(const void* offs, int is64, int64_t B, int outer, int H, void* ws,
+                          cudaStream_t stream);
+
+// Device side: item -> (seq, head, j) with j the rank of the tile within its
+// (seq, head) group (0 = first scheduled).
+struct WorkItem {
+  int32_t seq, head, j, ntiles;
+};
+__device__ __forceinline__ WorkItem decode_item(const void* ws, int64_t B, int H, int64_t item) {
+  const SeqRef* refs = reinterpret_cast<const SeqRef*>(reinterpret_cast<const char*>(ws) + 16);
+  int64_t lo = 0, hi = B - 1;
+  while (lo < hi) {  // last entry with item_start <= item
+    const int64_t mid = (lo + hi + 1) >> 1;
+    if (refs[mid].item_start <= item) lo = mid; else hi = mid - 1;
+  }
+  // Skip empty sequences that share item_start with the owner.
+  while (lo < B - 1 && refs[lo].ntiles == 0) ++lo;
+  const SeqRef r = refs[lo];
+  const int64_t i = item - r.item_start;
+  WorkItem w;
+  w.seq = r.seq;
+  w.ntiles = r.ntiles;
+  w.head = (int32_t)(i / r.ntiles);
+  w.j = (int32_t)(i % r.ntiles);
+  (void)H;
+  return w;
+}
+__device__ __forceinline__ int64_t total_items(const void* ws) {
+  return *reinterpret_cast<const int64_t*>(ws);
+}
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point, so the
 // library does not link libcuda directly.
@@ -47,5 +78,10 @@ EncodeTiledFn get_encode_tiled();
 int make_thd_map(CUtensorMap* map, const void* base, int64_t T, int64_t H, int D,
                  int64_t row_stride, int64_t head_stride, int box_d, int box_rows, int swizzle_bytes,
                  bool bf16);
+
+// Tensor map over a packed (T, H, D) fp32 tensor (row-major, contiguous), box
+// {D, 1, box_rows}, no swizzle; used as the target of TMA reduce-adds.
+int make_thd_map_f32(CUtensorMap* map, const void* base, int64_t T, int64_t H, int D,
+                     int box_rows);
 
 }  // namespace scree

@@ -55,8 +55,8 @@ struct FwdParams {
   int H;
   int T;
   float scale_log2;
-  const int32_t* tile_count;
-  const TileRef* tiles;
+  const void* sched;  // schedule (attn_common.cuh)
+  int64_t B;
   int* status;  // device status word
   void* o;
   int64_t o_rs, o_hs;
@@ -111,16 +111,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t IDESC_S = make_idesc_f16(BM, BN, kBF16, false, false);
   constexpr uint32_t IDESC_O = make_idesc_f16(BM, D, kBF16, false, true);
 
-  const int item = blockIdx.x;
-  const int ntiles = *p.tile_count;
-  if (item >= ntiles * p.H) return;
+  const int64_t item = blockIdx.x;
+  if (item >= total_items(p.sched)) return;
   // A CTA of an earlier failed launch (or of this one) set the status word: skip.
   if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
-  const TileRef tr = p.tiles[item / p.H];
-  const int h = item % p.H;
-  const int64_t seq_start = load_offset(p.offs, p.is64, tr.seq);
-  const int L = (int)(load_offset(p.offs, p.is64, tr.seq + 1) - seq_start);
-  const int q0 = tr.tile * BM;
+  const WorkItem wi = decode_item(p.sched, p.B, p.H, item);
+  const int h = wi.head;
+  const int64_t seq_start = load_offset(p.offs, p.is64, wi.seq);
+  const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - seq_start);
+  // Causal: heaviest (last) query tile first within each (sequence, head).
+  const int q0 = (CAUSAL ? (wi.ntiles - 1 - wi.j) : wi.j) * BM;
   const int nk_all = (L + BN - 1) / BN;
   const int n_kv = CAUSAL ? min(nk_all, (q0 + BM - 1) / BN + 1) : nk_all;
 
@@ -390,7 +390,7 @@ using namespace scree;
 extern "C" size_t scree_attn_fwd_workspace_size(int64_t B, int64_t T, int64_t H, int D) {
   (void)H;
   (void)D;
-  return schedule_bytes(B, T, BM);
+  return schedule_bytes(B);
 }
 
 extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64_t q_rs,
@@ -410,7 +410,7 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
   SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16, "attn_fwd: fp16 or bf16 only");
   if (T == 0) return SCREE_OK;
   SCREE_CHECK_ARG(q && k && v && o && offsets, "attn_fwd: null pointer");
-  SCREE_CHECK_ARG(workspace && workspace_bytes >= schedule_bytes(B, T, BM),
+  SCREE_CHECK_ARG(workspace && workspace_bytes >= schedule_bytes(B),
                   "attn_fwd: workspace too small");
   SCREE_CHECK_ARG(((uintptr_t)o % 16) == 0 && (o_rs % 8) == 0 && (o_hs % 8) == 0,
                   "attn_fwd: output must be 16-byte aligned with strides multiple of 8");
@@ -423,17 +423,16 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
   if ((rc = make_thd_map(&tq, q, T, H, D, q_rs, q_hs, swb / 2, BM, swb, bf16))) return rc;
   if ((rc = make_thd_map(&tk, k, T, H, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
   if ((rc = make_thd_map(&tv, v, T, H, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
-  if ((rc = launch_build_schedule(offsets, offs_is_i64, B, BM, BN, causal, 0, workspace, s)))
-    return rc;
+  if ((rc = launch_build_schedule(offsets, offs_is_i64, B, BM, (int)H, workspace, s))) return rc;
   FwdParams p;
   p.offs = offsets;
   p.is64 = offs_is_i64;
   p.H = (int)H;
   p.T = (int)T;
   p.scale_log2 = scale * 1.4426950408889634f;
-  p.tile_count = reinterpret_cast<const int32_t*>(workspace);
+  p.sched = workspace;
+  p.B = B;
   p.status = device_status_ptr();
-  p.tiles = reinterpret_cast<const TileRef*>((const char*)workspace + 16);
   p.o = o;
   p.o_rs = o_rs;
   p.o_hs = o_hs;

@@ -44,3 +44,44 @@ def attn_reference(q, k, v, do, lengths, causal, heads=None):
 
 def max_err(a, b):
     return float(np.max(np.abs(np.asarray(a, dtype=np.float64) - np.asarray(b, dtype=np.float64)))) if np.size(a) else 0.0
+
+
+def round_to(x, dtype):
+    """Round float64 values to a torch 16-bit dtype and back."""
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dtype).double().numpy()
+
+
+def attn_bwd_emulated(do, q, k, v, lengths, causal, dtype):
+    """Oracle backward evaluated with the 16-bit rounding points every tensor-core
+    attention backward has (scree's Triton kernel included:
+    triton/_backward.py:174, :181, :282): the forward output O is stored in
+    `dtype` before Delta = rowsum(O * dO), and P and dS are rounded to `dtype`
+    before their GEMMs.  Everything else is float64."""
+    import math as _m
+
+    qn, kn, vn, don = (to64(t) for t in (q, k, v, do))
+    offs = offsets_np(lengths)
+    out, _ = oracle.attention_fwd(qn, kn, vn, offs, causal=causal)
+    out = round_to(out, dtype)
+    scale = 1.0 / _m.sqrt(qn.shape[-1])
+    dq, dk, dv = np.zeros_like(qn), np.zeros_like(kn), np.zeros_like(vn)
+    for i in range(len(offs) - 1):
+        s0, e0 = int(offs[i]), int(offs[i + 1])
+        if e0 == s0:
+            continue
+        qh, kh, vh, doh, oh = (t[s0:e0].transpose(1, 0, 2) for t in (qn, kn, vn, don, out))
+        sc = np.matmul(qh, kh.transpose(0, 2, 1)) * scale
+        if causal:
+            L = e0 - s0
+            sc = np.where(np.triu(np.ones((L, L), dtype=bool), k=1), -np.inf, sc)
+        m = sc.max(-1, keepdims=True)
+        P = np.exp(sc - m)
+        P /= P.sum(-1, keepdims=True)
+        delta = (oh * doh).sum(-1, keepdims=True)
+        Pr = round_to(P, dtype)
+        dv[s0:e0] = np.matmul(Pr.transpose(0, 2, 1), doh).transpose(1, 0, 2)
+        dP = np.matmul(doh, vh.transpose(0, 2, 1))
+        dS = round_to(P * (dP - delta), dtype)
+        dq[s0:e0] = (scale * np.matmul(dS, kh)).transpose(1, 0, 2)
+        dk[s0:e0] = (scale * np.matmul(dS.transpose(0, 2, 1), qh)).transpose(1, 0, 2)
+    return dq, dk, dv

@@ -4,6 +4,14 @@ Bar: |got - ref| <= atol + rtol |ref| for out, dq, dk, dv against the fp64
 oracle run on the same 16-bit inputs, atol = 2e-3 (fp16) / 1e-2 (bf16) and
 rtol = the output dtype's half-ulp (2^-12 fp16, 2^-9 bf16, written here as one
 ulp of headroom: 2^-11 / 2^-8); LSE (fp32) within 1e-3 absolute.
+
+For the gradients there is a second, FlashAttention-style criterion: a
+tensor-core backward must feed P and dS to its GEMMs in 16 bits (so does
+scree's Triton backward, triton/_backward.py:174, :181, :282), and that
+rounding alone can exceed the flat bound on long rows.  A gradient passes if it
+meets the bound above OR its max error is at most twice the max error of the
+fp64 oracle evaluated with exactly those 16-bit rounding points
+(gpu_helpers.attn_bwd_emulated).
 """
 
 import math
@@ -14,7 +22,7 @@ import torch
 
 import oracle
 from conftest import decode16, load_golden
-from gpu_helpers import ATTN_REL, ATTN_TOL, attn_reference, excess, max_err, to64
+from gpu_helpers import ATTN_REL, ATTN_TOL, attn_bwd_emulated, attn_reference, excess, max_err, to64
 
 pytestmark = pytest.mark.gpu
 
@@ -44,7 +52,19 @@ def _check(lengths, H, D, dtype, causal, device, heads=None, seed=0, check_bwd=T
         g = to64(got[:, sl])
         errs[name] = max_err(g, want)
         over[name] = excess(g, want, 1e-3, 0.0) if name == "lse" else excess(g, want, tol, rel)
+    emul = None
     for name, e in over.items():
+        if e > 0 and name in ("dq", "dk", "dv"):
+            if emul is None:
+                sub = [t[:, sl] for t in ins]
+                emul = dict(zip(("dq", "dk", "dv"), attn_bwd_emulated(*sub, lengths, causal, dtype)))
+            want = ref[names.index(name)]
+            e_emul = max_err(emul[name], want)
+            assert errs[name] <= 2 * e_emul, (
+                f"{name}: max err {errs[name]:.3e} exceeds the bound by {e:.3e} and twice the "
+                f"16-bit-operand emulation's error {e_emul:.3e} (all: {errs})"
+            )
+            continue
         assert e <= 0, f"{name}: out of bounds by {e:.3e} (max abs errors {errs})"
     from scree_b200 import _lib
 
