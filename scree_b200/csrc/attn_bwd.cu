@@ -302,9 +302,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           issue_s_dp(it + 1, true);
         }
-        // dK += dS^T Q_i ; dQ_i
+        // dS_i published: the softmax warps are done reading dP_i, so dP_{i+1}
+        // goes first and their next dS phase waits on one GEMM, not three.
         if (!(ok = mbar_wait(ds_full, it & 1, abort_flag, p.status, 26))) break;
         tc_fence_after();
+        if (more) issue_s_dp(it + 1, false);
+        // dK += dS^T Q_i ; dQ_i
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
           umma_f16_ss(tmem + C::COL_DK, pt_kmaj(sDS, kk), mnmaj<D>(qb, BQ, kk), ID_ACC,
@@ -323,7 +326,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(dq_full);
         umma_commit(ds_free);
         umma_commit(&q_empty[st]);
-        if (more) issue_s_dp(it + 1, false);
       }
       umma_commit(acc_done);
     }

@@ -267,9 +267,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BN; ++c)
           if (k0 + c > lim) s[c] = -INFINITY;
       }
-      float mx = s[0];
+      // Row max with 8 independent chains (a single 128-long chain would cost
+      // ~128 x FMNMX latency with one warp per scheduler).
+      float mx8[8];
 #pragma unroll
-      for (int c = 1; c < BN; ++c) mx = fmaxf(mx, s[c]);
+      for (int a = 0; a < 8; ++a) mx8[a] = s[a];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_cand = mx * sl2;
       float alpha = 1.f;
       bool need = false;
@@ -283,12 +289,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_used = m_cand;
       }
       const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
-      float rs = 0.f;
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BN; ++c) {
         s[c] = ex2_approx(fmaf(s[c], sl2, -m_eff));
-        rs += s[c];
+        rs8[c & 7] += s[c];
       }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       if (j >= 1) {
         ok = mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status, 8);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }

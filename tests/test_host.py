@@ -56,7 +56,7 @@ def test_workspace_sizes():
     T, H, D, B = 158330, 32, 128, 64
     ws = lib.scree_attn_bwd_workspace_size(B, T, H, D)
     assert ws >= T * H * D * 4 + 2 * T * H * 4
-    assert lib.scree_attn_fwd_workspace_size(B, T, H, D) >= 16 + 8 * (T // 128 + B)
+    assert lib.scree_attn_fwd_workspace_size(B, T, H, D) == 16 + 16 * B  # one schedule entry per sequence
 
 
 def test_workloads_match_documented_sizes():
