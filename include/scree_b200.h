@@ -75,6 +75,23 @@ int scree_attn_fwd(const void* q, const void* k, const void* v, int64_t q_row_st
                    int64_t o_head_stride, float* lse, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* Allocation-free variant of scree_attn_fwd (no counterpart in the reference).
+ * For callers that cannot allocate device memory when they run attention (an
+ * engine with a fixed pre-planned memory arena, or a binding that only holds
+ * raw input/output pointers): same arguments and results as scree_attn_fwd
+ * minus the workspace, which comes from a 64 KiB array built into the library
+ * (one per GPU, held until process exit).  Limit: B <= 4095 sequences, larger
+ * batches return SCREE_ERR_INVALID.  All calls on a device share that array:
+ * calls that overlap on the GPU race, so order them (one stream).  The first
+ * call on a device resolves the array's address; make it before any stream
+ * capture.  Allocates nothing. */
+int scree_attn_fwd_noalloc(const void* q, const void* k, const void* v, int64_t q_row_stride,
+                           int64_t q_head_stride, int64_t k_row_stride, int64_t k_head_stride,
+                           int64_t v_row_stride, int64_t v_head_stride, const void* offsets,
+                           int offs_is_i64, int64_t B, int64_t T, int64_t H, int D, int dtype,
+                           int causal, float scale, int64_t max_seqlen, void* o,
+                           int64_t o_row_stride, int64_t o_head_stride, float* lse, void* stream);
+
 /* Varlen self-attention backward: dq, dk, dv from do, q, k, v, o, lse.
  * Replaces: scree/kernels/triton/_backward.py:288-396
  *   varlen_attention_triton_backward(do, q, k, v, o, lse, cu_seqlens, causal,

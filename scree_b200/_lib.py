@@ -38,6 +38,10 @@ _SIGNATURES = {
         _I,
         [_P, _P, _P, _L, _L, _L, _L, _L, _L, _P, _I, _L, _L, _L, _I, _I, _I, _F, _L, _P, _L, _L, _P, _P, _S, _P],
     ),
+    "scree_attn_fwd_noalloc": (
+        _I,
+        [_P, _P, _P, _L, _L, _L, _L, _L, _L, _P, _I, _L, _L, _L, _I, _I, _I, _F, _L, _P, _L, _L, _P, _P],
+    ),
     "scree_attn_bwd_workspace_size": (_S, [_L, _L, _L, _I]),
     "scree_attn_bwd": (
         _I,

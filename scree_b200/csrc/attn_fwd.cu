@@ -460,3 +460,65 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
 #undef SCREE_FWD_CASE
   return SCREE_ERR_UNSUPPORTED;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of scree_attn_fwd.
+//
+// Some callers cannot allocate device memory at the point where they run
+// attention: an inference engine or plugin host that owns a fixed,
+// pre-planned memory arena and forbids allocation after start-up, or code whose
+// allocator is not reachable from the C side at all (a foreign-language binding
+// that only holds raw pointers to inputs and outputs).  For them this entry
+// point takes the forward's only scratch, the work schedule (16 bytes per
+// sequence plus a 16-byte header), from a fixed array compiled into the
+// library instead of a caller-provided workspace.
+//
+// Limits and rules:
+//  * The array holds kNoAllocScratchBytes = 64 KiB per GPU that loads the
+//    library, for as long as the process lives, so at most
+//    (64 KiB - 16) / 16 = 4095 sequences per call; larger batches are rejected
+//    with SCREE_ERR_INVALID before any work is enqueued.
+//  * All calls on a device share the one array.  The schedule kernel rewrites
+//    every byte the attention kernel later reads, so nothing has to start at
+//    zero, but two calls whose work overlaps on the GPU (different streams
+//    without ordering between them) race on the array and give wrong results.
+//    Serialise them, e.g. issue them on one stream.
+//  * The first call on each device looks up the array's device address
+//    (cudaGetSymbolAddress, with that device current); make that first call
+//    before any stream capture.  Later calls reuse the cached address.
+// It allocates nothing itself: no cudaMalloc, cudaFree or allocating library
+// routine, and it then runs exactly the scree_attn_fwd path.
+namespace {
+constexpr size_t kNoAllocScratchBytes = 64 * 1024;
+static __device__ __align__(256) unsigned char g_fwd_noalloc_scratch[kNoAllocScratchBytes];
+}  // namespace
+
+extern "C" int scree_attn_fwd_noalloc(const void* q, const void* k, const void* v, int64_t q_rs,
+                                      int64_t q_hs, int64_t k_rs, int64_t k_hs, int64_t v_rs,
+                                      int64_t v_hs, const void* offsets, int offs_is_i64,
+                                      int64_t B, int64_t T, int64_t H, int D, int dtype,
+                                      int causal, float scale, int64_t max_seqlen, void* o,
+                                      int64_t o_rs, int64_t o_hs, float* lse, void* stream) {
+  SCREE_CHECK_ARG(B >= 1, "attn_fwd_noalloc: bad batch size %lld", (long long)B);
+  SCREE_CHECK_ARG(schedule_bytes(B) <= kNoAllocScratchBytes,
+                  "attn_fwd_noalloc: %lld sequences exceed the built-in scratch limit of %lld "
+                  "(64 KiB); use scree_attn_fwd with a caller workspace",
+                  (long long)B, (long long)((kNoAllocScratchBytes - 16) / 16));
+  if (T == 0) return SCREE_OK;
+  SCREE_CHECK_ARG(q != nullptr, "attn_fwd_noalloc: null q");
+  // Make the device that owns the stream (or q) current, then resolve the
+  // array's address on that device once.
+  SCREE_BIND_DEVICE(stream, q);
+  static void* scratch_ptr[64] = {nullptr};
+  int dev = 0;
+  SCREE_CUDA_TRY(cudaGetDevice(&dev));
+  SCREE_CHECK_ARG(dev >= 0 && dev < 64, "attn_fwd_noalloc: device index %d out of range", dev);
+  if (scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    SCREE_CUDA_TRY(cudaGetSymbolAddress(&p, g_fwd_noalloc_scratch));
+    scratch_ptr[dev] = p;
+  }
+  return scree_attn_fwd(q, k, v, q_rs, q_hs, k_rs, k_hs, v_rs, v_hs, offsets, offs_is_i64, B, T,
+                        H, D, dtype, causal, scale, max_seqlen, o, o_rs, o_hs, lse,
+                        scratch_ptr[dev], kNoAllocScratchBytes, stream);
+}
