@@ -229,10 +229,17 @@ def run_reference_arm(args, lengths, H, D, causal):
     print(json.dumps(line), flush=True)
 
 
+_LEN_DESC = {
+    "cfg2": "lognormal(ln 700, 0.6) rescaled to 12160 tokens",
+    "cfg4": "lognormal(ln 2048, 0.6) clip [16,16384]",
+    "cfg5": "lognormal(ln 1024, 1.2) clip [1,32768], 4 forced length-1",
+}
+
+
 def workload_config(args, lengths, H, D, causal, world):
     return {
-        "workload": f"{args.config}: {len(lengths)} seqs lognormal(ln 2048, 0.6) clip [16,16384] seed 0, "
-        f"T={sum(lengths)}, H={H}, D={D}, bf16, {'causal' if causal else 'non-causal'} fwd+bwd",
+        "workload": f"{args.config}: {len(lengths)} seqs {_LEN_DESC[args.config]} seed 0, "
+        f"T={sum(lengths)}, H={H}, D={D}, {getattr(args, 'dtype_name', 'bfloat16')}, {'causal' if causal else 'non-causal'} fwd+bwd",
         "global_batch": int(sum(lengths)),
         "seqs": len(lengths),
         "max_seqlen": int(max(lengths)),
@@ -255,6 +262,7 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--non-causal", action="store_true")
     ap.add_argument("--max-seqs", type=int, default=0, help="keep only the first N sequences (small profiling case)")
     args = ap.parse_args()
 
@@ -264,7 +272,8 @@ def main():
     lengths = list(cfg.lengths)
     if args.max_seqs:
         lengths = lengths[: args.max_seqs]
-    H, D, causal = cfg.heads, cfg.head_dim, cfg.causal
+    H, D, causal = cfg.heads, cfg.head_dim, cfg.causal and not args.non_causal
+    args.dtype_name = "float16" if cfg.dtype == "float16" else "bfloat16"
 
     if args.impl == "reference":
         run_reference_arm(args, lengths, H, D, causal)
@@ -292,7 +301,7 @@ def main():
         assert obj[0] == plan, "shard plan differs across ranks"
     mine = [lengths[i] for i in plan[rank]]
     T = sum(mine)
-    dt = torch.bfloat16
+    dt = getattr(torch, args.dtype_name)
     g = torch.Generator(device=dev).manual_seed(1234 + 17 * rank)
 
     def rnd():
@@ -433,7 +442,7 @@ def main():
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": "f16" if args.dtype_name == "float16" else "bf16",
             "data": "synthetic",
             "config": workload_config(args, lengths, H, D, causal, world),
             "tflops": tflops,

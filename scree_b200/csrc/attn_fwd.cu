@@ -6,9 +6,9 @@
 // One CTA owns one 128-row query tile of one head and streams the sequence's
 // 128-key tiles through a TMA -> tcgen05.mma pipeline:
 //
-//   warp 4  (TMA)      Q once; K_j, V_j into a STAGES-deep ring (mbarrier tx)
-//   warp 5  (MMA)      S_j = Q K_j^T into TMEM buffer j%2, then O += P_{j-1} V_{j-1}
-//   warps 0-3 (softmax) thread r owns query row r == TMEM lane r: reads S_j,
+//   warp 8  (TMA)      Q once; K_j and V_j into separate rings (mbarrier tx)
+//   warp 9  (MMA)      S_j = Q K_j^T into TMEM buffer j%2, then O += P_{j-1} V_{j-1}
+//   warps 0-7 (softmax) warps w, w+4 own query rows 32(w%4).. (TMEM lanes), one half of the key columns each: read S_j,
 //                      masks, keeps running max/sum in registers, writes P_j
 //                      (bf16/fp16, 128B-swizzled K-major) to shared memory,
 //                      rescales O in TMEM only when the max grew by more than
@@ -26,7 +26,7 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BN = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // 8 softmax warps, TMA warp, MMA warp
 
 template <int D>
 struct FwdCfg {
@@ -34,18 +34,26 @@ struct FwdCfg {
   static constexpr int CHUNK = SWB / 2;           // elements per swizzle row
   static constexpr int NCHUNK = D / CHUNK;
   static constexpr uint32_t SWZ = SWB == 128 ? SW_128B : SW_64B;
-  static constexpr int STAGES = D == 128 ? 2 : 3;
+  // K is released right after S = Q K^T, V only after O += P V, so they have
+  // separate rings; K gets the deeper one because S_{j} is issued first.
+  static constexpr int KSTAGES = 3;
+  static constexpr int VSTAGES = D == 128 ? 2 : 3;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int P_BYTES = BM * BN * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
-  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-  // barriers + alignment slack; at least 120 KB so that two CTAs (each holding
-  // all 512 TMEM columns) never share an SM.
-  static constexpr int SMEM_RAW = OFF_BAR + 256 + 1024;
+  static constexpr int OFF_V = OFF_K + KSTAGES * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + VSTAGES * KV_BYTES;
+  // One P buffer: the softmax writes P_j only after O += P_{j-1} V_{j-1} completed
+  // (it must wait for that anyway before rescaling O).
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int OFF_RED = OFF_BAR + 192;           // [2 parity][2 half][BM] fp32
+  static constexpr int OFF_END = OFF_RED + 2 * 2 * BM * 4;
+  // 1 KB of alignment slack when it fits; the kernel checks the real alignment.
+  static constexpr int SMEM_RAW = OFF_END + 1024 <= 232448 ? OFF_END + 1024 : OFF_END;
+  // At least 120 KB so that two CTAs (each holding all 512 TMEM columns) never
+  // share an SM.
   static constexpr int SMEM = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
 };
 
@@ -127,20 +135,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  {
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    if ((uint32_t)(smem - smem_raw) + (uint32_t)C::OFF_END > dyn) {
+      if (threadIdx.x == 0) record_device_error(p.status, SCREE_DEVERR_BAD_INPUT, 90);
+      return;
+    }
+  }
   const uint32_t sQ = smem_u32(smem + C::OFF_Q);
   const uint32_t sK = smem_u32(smem + C::OFF_K);
   const uint32_t sV = smem_u32(smem + C::OFF_V);
   const uint32_t sP = smem_u32(smem + C::OFF_P);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;                  // [STAGES]
-  uint64_t* v_full = k_full + C::STAGES;        // [STAGES]
-  uint64_t* kv_empty = v_full + C::STAGES;      // [STAGES]
-  uint64_t* s_full = kv_empty + C::STAGES;      // [2]
+  uint64_t* k_full = bars + 1;                  // [KSTAGES]
+  uint64_t* k_empty = k_full + C::KSTAGES;      // [KSTAGES]
+  uint64_t* v_full = k_empty + C::KSTAGES;      // [VSTAGES]
+  uint64_t* v_empty = v_full + C::VSTAGES;      // [VSTAGES]
+  uint64_t* s_full = v_empty + C::VSTAGES;      // [2]
   uint64_t* s_empty = s_full + 2;               // [2]
   uint64_t* p_full = s_empty + 2;               // [2]
   uint64_t* pv_done = p_full + 2;               // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* xch = pv_done + 2;                  // [2] row-max exchange between column halves
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xch + 2);
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -148,22 +167,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < C::STAGES; ++s) {
+    for (int s = 0; s < C::KSTAGES; ++s) {
       mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < C::VSTAGES; ++s) {
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 128);
-      mbar_init(&p_full[b], 128);
+      mbar_init(&s_empty[b], 256);
+      mbar_init(&p_full[b], 256);
       mbar_init(&pv_done[b], 1);
+      mbar_init(&xch[b], 256);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) tmem_alloc<512>(tmem_slot);
-  if (warp == 4 && lane == 0) {
+  if (warp == 9) tmem_alloc<512>(tmem_slot);
+  if (warp == 8 && lane == 0) {
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
@@ -173,24 +196,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
-    if (elect_one()) {
-      const int row0 = (int)seq_start;
+    // Lane 0 streams Q and the K ring, lane 1 the V ring, each at its own pace.
+    const int row0 = (int)seq_start;
+    if (lane == 0) {
       mbar_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
       for (int c = 0; c < C::NCHUNK; ++c)
         tma_load_3d(smem + C::OFF_Q + c * BM * C::SWB, &tm_q, q_full, c * C::CHUNK, h, row0 + q0);
       for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::STAGES;
-        if (j >= C::STAGES &&
-            !mbar_wait(&kv_empty[st], ((j / C::STAGES) - 1) & 1, abort_flag, p.status, 1))
+        const int st = j % C::KSTAGES;
+        if (j >= C::KSTAGES &&
+            !mbar_wait(&k_empty[st], ((j / C::KSTAGES) - 1) & 1, abort_flag, p.status, 1))
           break;
         mbar_expect_tx(&k_full[st], C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c)
           tma_load_3d(smem + C::OFF_K + st * C::KV_BYTES + c * BN * C::SWB, &tm_k, &k_full[st],
                       c * C::CHUNK, h, row0 + j * BN);
+      }
+    } else if (lane == 1) {
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % C::VSTAGES;
+        if (j >= C::VSTAGES &&
+            !mbar_wait(&v_empty[st], ((j / C::VSTAGES) - 1) & 1, abort_flag, p.status, 12))
+          break;
         mbar_expect_tx(&v_full[st], C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c)
@@ -198,28 +229,28 @@ __global__ void __launch_bounds__(kThreads, 1)
                       c * C::CHUNK, h, row0 + j * BN);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
       auto issue_pv = [&](int i) -> bool {
-        const int b2 = i & 1, st = i % C::STAGES;
+        const int b2 = i & 1, st = i % C::VSTAGES;
         if (!mbar_wait(&p_full[b2], (i >> 1) & 1, abort_flag, p.status, 2)) return false;
-        if (!mbar_wait(&v_full[st], (i / C::STAGES) & 1, abort_flag, p.status, 3)) return false;
+        if (!mbar_wait(&v_full[st], (i / C::VSTAGES) & 1, abort_flag, p.status, 3)) return false;
         tc_fence_after();
-        const uint32_t pb = sP + b2 * C::P_BYTES;
+        const uint32_t pb = sP;
         const uint32_t vb = sV + st * C::KV_BYTES;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
           umma_f16_ss(tmem + 256, p_desc(pb, kk), v_desc<D>(vb, kk), IDESC_O,
                       (i > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&pv_done[b2]);
-        umma_commit(&kv_empty[st]);
+        umma_commit(&v_empty[st]);
         return true;
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 4);
       for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % C::STAGES, b2 = j & 1;
-        if (!mbar_wait(&k_full[st], (j / C::STAGES) & 1, abort_flag, p.status, 5)) { ok = false; break; }
+        const int st = j % C::KSTAGES, b2 = j & 1;
+        if (!mbar_wait(&k_full[st], (j / C::KSTAGES) & 1, abort_flag, p.status, 5)) { ok = false; break; }
         if (j >= 2 && !mbar_wait(&s_empty[b2], ((j - 2) >> 1) & 1, abort_flag, p.status, 6)) {
           ok = false;
           break;
@@ -231,51 +262,64 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16_ss(tmem + b2 * BN, kmajor_desc<D>(sQ, BM, kk), kmajor_desc<D>(kb, BN, kk),
                       IDESC_S, kk > 0 ? 1u : 0u);
         umma_commit(&s_full[b2]);
+        umma_commit(&k_empty[st]);
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok && n_kv > 0) issue_pv(n_kv - 1);
     }
   } else {
     // ------------------------------------------------------------ softmax warps
-    const int r = threadIdx.x;  // query row within the tile == TMEM lane
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    const int qi = q0 + r;      // query index within the sequence
+    // Warps w and w+4 share TMEM lanes 32*(w%4)..+31 (query rows); warp w < 4
+    // takes key columns [0,64) of each tile, warp w+4 columns [64,128).  The two
+    // halves exchange their row maxima once per tile (mbarrier xch, so the wait
+    // stays bounded) and their partial sums once at the end.
+    const int hf = warp >> 2;                 // column half
+    const int r = (warp & 3) * 32 + lane;     // query row within the tile == TMEM lane
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+    const int qi = q0 + r;                    // query index within the sequence
     const float sl2 = p.scale_log2;
-    float m_used = -INFINITY;   // running max, scaled log2 units
-    float l = 0.f;
+    constexpr int HN = BN / 2;                // columns per half
+    float m_used = -INFINITY;                 // running max, scaled log2 units
+    float l = 0.f;                            // partial sum over this half's columns
     bool ok = true;
-    uint8_t* prow_base = smem + C::OFF_P + r * 128;
+    uint8_t* prow_base = smem + C::OFF_P + hf * BM * 128 + r * 128;
     const int sw = r & 7;
     for (int j = 0; j < n_kv; ++j) {
       const int b2 = j & 1;
       ok = mbar_wait(&s_full[b2], (j >> 1) & 1, abort_flag, p.status, 7);
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
-      float s[BN];
+      float s[HN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        tmem_ld32(lane_base + b2 * BN + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      for (int c = 0; c < HN / 32; ++c)
+        tmem_ld32(lane_base + b2 * BN + hf * HN + c * 32,
+                  *reinterpret_cast<float(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_empty[b2]);
 
-      const int k0 = j * BN;
-      const bool need_mask = (k0 + BN > L) || (CAUSAL && k0 + BN - 1 > q0);
+      const int k0 = j * BN + hf * HN;
+      const bool need_mask = (j * BN + BN > L) || (CAUSAL && j * BN + BN - 1 > q0);
       if (need_mask) {
         const int lim = CAUSAL ? min(L - 1, qi) : (L - 1);  // last valid key
 #pragma unroll
-        for (int c = 0; c < BN; ++c)
+        for (int c = 0; c < HN; ++c)
           if (k0 + c > lim) s[c] = -INFINITY;
       }
-      // Row max with 8 independent chains (a single 128-long chain would cost
-      // ~128 x FMNMX latency with one warp per scheduler).
+      // Row max: 8 independent chains, then the other half's value.
       float mx8[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx8[a] = s[a];
 #pragma unroll
-      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int c = 8; c < HN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      red[(b2 * 2 + hf) * BM + r] = mx;
+      mbar_arrive(&xch[b2]);
+      ok = mbar_wait(&xch[b2], (j >> 1) & 1, abort_flag, p.status, 10);
+      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+      mx = fmaxf(mx, red[(b2 * 2 + (hf ^ 1)) * BM + r]);
+      // Both halves now see the same max, so their lazy-rescale decisions agree.
       const float m_cand = mx * sl2;
       float alpha = 1.f;
       bool need = false;
@@ -291,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
       float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < BN; ++c) {
+      for (int c = 0; c < HN; ++c) {
         s[c] = ex2_approx(fmaf(s[c], sl2, -m_eff));
         rs8[c & 7] += s[c];
       }
@@ -301,8 +345,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffff, need)) {
+          // O columns in 32-wide chunks; chunk c belongs to half c % 2.
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
+            if ((c & 1) != hf) continue;
             float o[32];
             tmem_ld32(lane_base + 256 + c * 32, o);
             tmem_wait_ld();
@@ -314,18 +360,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       l = l * alpha + rs;
-      // P row -> shared memory, 128B swizzle: 16-byte unit u of row r lives at
-      // unit position u ^ (r % 8) within its 128-byte row.
-      uint8_t* prow = prow_base + b2 * C::P_BYTES;
+      // This half's 64 keys are one 128-byte swizzled column block of P:
+      // 16-byte unit u of row r lives at unit position u ^ (r % 8).
+      uint8_t* prow = prow_base;
 #pragma unroll
-      for (int u = 0; u < BN / 8; ++u) {
+      for (int u = 0; u < HN / 8; ++u) {
         uint4 w;
         w.x = Pk2<T>::pack(s[u * 8 + 0], s[u * 8 + 1]);
         w.y = Pk2<T>::pack(s[u * 8 + 2], s[u * 8 + 3]);
         w.z = Pk2<T>::pack(s[u * 8 + 4], s[u * 8 + 5]);
         w.w = Pk2<T>::pack(s[u * 8 + 6], s[u * 8 + 7]);
-        const int blk = u >> 3, uu = u & 7;
-        *reinterpret_cast<uint4*>(prow + blk * BM * 128 + ((uu ^ sw) << 4)) = w;
+        *reinterpret_cast<uint4*>(prow + ((u ^ sw) << 4)) = w;
       }
       fence_proxy_async_smem();
       tc_fence_before();
@@ -337,12 +382,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffff, ok);
     }
     if (ok && n_kv > 0) {
+      // Total row sum: exchange the partial sums through the exchange buffer of
+      // the parity the last tile did not use (its readers have moved on).
+      const int pb = n_kv & 1;
+      red[(pb * 2 + hf) * BM + r] = l;
+      mbar_arrive(&xch[pb]);
+      ok = mbar_wait(&xch[pb], (n_kv >> 1) & 1, abort_flag, p.status, 11);
+      ok = __all_sync(0xffffffff, ok);
+      if (ok) l += red[(pb * 2 + (hf ^ 1)) * BM + r];
+    }
+    if (ok && n_kv > 0) {
       tc_fence_after();
       const bool row_ok = qi < L;
       const float inv_l = 1.0f / l;
       T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
+        if ((c & 1) != hf) continue;
         float o[32];
         tmem_ld32(lane_base + 256 + c * 32, o);
         tmem_wait_ld();
@@ -358,14 +414,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (row_ok && p.lse != nullptr)
+      if (hf == 0 && row_ok && p.lse != nullptr)
         p.lse[(seq_start + qi) * p.H + h] = (m_used + log2f(l)) * 0.69314718055994531f;
     }
   }
 
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc<512>(tmem);
   }
