@@ -3,29 +3,46 @@
 // Computes, per sequence b and head h (reference/varlen_attention.py:121-138):
 //   S = Q K^T * scale, causal mask k > q -> -inf, P = softmax(S), O = P V,
 //   LSE = m + ln(l)  (natural log; triton/varlen_attention.py:160)
-// One CTA owns one 128-row query tile of one head and streams the sequence's
-// 128-key tiles through a TMA -> tcgen05.mma pipeline:
 //
-//   warp 8  (TMA)      Q once; K_j and V_j into separate rings (mbarrier tx)
-//   warp 9  (MMA)      S_j = Q K_j^T into TMEM buffer j%2, then O += P_{j-1} V_{j-1}
-//   warps 0-7 (softmax) warps w, w+4 own query rows 32(w%4).. (TMEM lanes), one half of the key columns each: read S_j,
-//                      masks, keeps running max/sum in registers, writes P_j
-//                      (bf16/fp16, 128B-swizzled K-major) to shared memory,
-//                      rescales O in TMEM only when the max grew by more than
-//                      2^8 (exact: P stays <= 256), and finally writes O / l, LSE.
+// One CTA owns 256 query rows of one head as two 128-row tiles, A and B, that
+// share every 128-key K/V tile the sequence streams through shared memory, so
+// each K/V byte feeds twice the tensor work of a single-tile CTA (the L2 -> SM
+// feed of K/V is what limits a 128-row CTA).
 //
-// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256+D).
+//   warp 8  (TMA)  lane 0: Q_A, Q_B once, then the K ring; lane 1: the V ring
+//   warp 9  (MMA)  one thread issues tcgen05.mma: S_X = Q_X K_j^T (X = A, B) and
+//                  O_X += P_X V_j, interleaved so the tensor core works on one
+//                  tile while the softmax warps of the other tile run
+//   warps 0-3      softmax of tile A, warps 4-7 softmax of tile B: thread r owns
+//                  query row r (= TMEM lane r), keeps the running max / sum in
+//                  registers, writes P (16-bit) back into TMEM, rescales O only
+//                  when the max grew by more than 2^8 (exact: P stays <= 256),
+//                  and finally stores O / l and the LSE.
+//
+// TMEM columns: S_A [0,128), S_B [128,256), O_A [256,256+D), O_B [256+D,256+2D).
+// P_X is written over the first 64 columns of S_X (two 16-bit values per
+// column) and read by O_X += P_X V_j straight from TMEM (A operand in TMEM).
+// Reuse is safe because one thread issues all MMAs and they execute in issue
+// order: S_X(j+1) is issued after O_X += P_X(j) V_j.
 // Softmax works in the exp2 domain with log2(e) folded into the scale.
 // Ragged tails: TMA reads whole 128-row boxes, so rows of the next sequence
 // arrive in K/V tiles; keys >= L are masked to -inf (P = 0), and query rows
 // >= L are computed but never stored.  Rows past T are zero-filled by TMA.
+#ifdef SCREE_TRACE
+// Profiling build only: per-site wait cycles (lane 0 of each waiting warp),
+// [30] = CTA lifetime cycles, [31] = key tiles processed.
+static __device__ unsigned long long g_fwd_trace[32];
+#define SCREE_TRACE_ADD(site, cyc) \
+  do { if ((threadIdx.x & 31) == 0 || (site) == 12) atomicAdd(&g_fwd_trace[(site) & 31], (unsigned long long)(cyc)); } while (0)
+#endif
 #include "attn_common.cuh"
 
 namespace scree {
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BM = 128;      // rows per query tile
+constexpr int ROWS = 2 * BM; // query rows per CTA (tiles A and B)
+constexpr int BN = 128;      // keys per K/V tile
 constexpr int kThreads = 320;  // 8 softmax warps, TMA warp, MMA warp
 
 template <int D>
@@ -34,27 +51,20 @@ struct FwdCfg {
   static constexpr int CHUNK = SWB / 2;           // elements per swizzle row
   static constexpr int NCHUNK = D / CHUNK;
   static constexpr uint32_t SWZ = SWB == 128 ? SW_128B : SW_64B;
-  // K is released right after S = Q K^T, V only after O += P V, so they have
-  // separate rings; K gets the deeper one because S_{j} is issued first.
   static constexpr int KSTAGES = 3;
   static constexpr int VSTAGES = D == 128 ? 2 : 3;
-  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int Q_BYTES = BM * D * 2;   // one query tile
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_Q = 0;              // Q_A, Q_B
+  static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KSTAGES * KV_BYTES;
-  static constexpr int OFF_P = OFF_V + VSTAGES * KV_BYTES;
-  // One P buffer: the softmax writes P_j only after O += P_{j-1} V_{j-1} completed
-  // (it must wait for that anyway before rescaling O).
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  static constexpr int OFF_RED = OFF_BAR + 192;           // [2 parity][2 half][BM] fp32
-  static constexpr int OFF_END = OFF_RED + 2 * 2 * BM * 4;
-  // 1 KB of alignment slack when it fits; the kernel checks the real alignment.
+  static constexpr int OFF_BAR = OFF_V + VSTAGES * KV_BYTES;
+  static constexpr int OFF_END = OFF_BAR + 192;
   static constexpr int SMEM_RAW = OFF_END + 1024 <= 232448 ? OFF_END + 1024 : OFF_END;
   // At least 120 KB so that two CTAs (each holding all 512 TMEM columns) never
   // share an SM.
   static constexpr int SMEM = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
+  static constexpr int COL_S = 0, COL_O = 256;  // S_X at COL_S + X*128, O_X at COL_O + X*D
 };
 
 struct FwdParams {
@@ -79,12 +89,6 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t base, int rows, int kk)
   const int e = kk * 16;
   const uint32_t addr = base + (e / C::CHUNK) * rows * C::SWB + (e % C::CHUNK) * 2;
   return make_sdesc(addr, 16, 8 * C::SWB, C::SWZ);
-}
-// P tile: [BM][BN] with 64-key 128-byte swizzled column blocks.
-__device__ __forceinline__ uint64_t p_desc(uint32_t base, int kk) {
-  const int e = kk * 16;
-  const uint32_t addr = base + (e / 64) * BM * 128 + (e % 64) * 2;
-  return make_sdesc(addr, 16, 1024, SW_128B);
 }
 // V as the MN-major B operand (N = D, K = keys): k-step kk covers keys
 // [16kk, 16kk+16) = 16 smem rows; D-chunks are BN*SWB bytes apart (LBO), groups of
@@ -127,10 +131,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h = wi.head;
   const int64_t seq_start = load_offset(p.offs, p.is64, wi.seq);
   const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - seq_start);
-  // Causal: heaviest (last) query tile first within each (sequence, head).
-  const int q0 = (CAUSAL ? (wi.ntiles - 1 - wi.j) : wi.j) * BM;
+  // Causal: heaviest (last) 256-row block first within each (sequence, head).
+  const int q0 = (CAUSAL ? (wi.ntiles - 1 - wi.j) : wi.j) * ROWS;
   const int nk_all = (L + BN - 1) / BN;
-  const int n_kv = CAUSAL ? min(nk_all, (q0 + BM - 1) / BN + 1) : nk_all;
+  // Key tiles each query tile needs (tile B may not exist at a sequence's end).
+  const int nA = CAUSAL ? min(nk_all, (q0 + BM - 1) / BN + 1) : nk_all;
+  const bool hasB = q0 + BM < L;
+  const int nB = !hasB ? 0 : (CAUSAL ? min(nk_all, (q0 + 2 * BM - 1) / BN + 1) : nk_all);
+  const int n_kv = max(nA, nB);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -146,24 +154,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sQ = smem_u32(smem + C::OFF_Q);
   const uint32_t sK = smem_u32(smem + C::OFF_K);
   const uint32_t sV = smem_u32(smem + C::OFF_V);
-  const uint32_t sP = smem_u32(smem + C::OFF_P);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;                  // [KSTAGES]
   uint64_t* k_empty = k_full + C::KSTAGES;      // [KSTAGES]
   uint64_t* v_full = k_empty + C::KSTAGES;      // [VSTAGES]
   uint64_t* v_empty = v_full + C::VSTAGES;      // [VSTAGES]
-  uint64_t* s_full = v_empty + C::VSTAGES;      // [2]
-  uint64_t* s_empty = s_full + 2;               // [2]
-  uint64_t* p_full = s_empty + 2;               // [2]
+  uint64_t* s_full = v_empty + C::VSTAGES;      // [2] per tile X
+  uint64_t* p_full = s_full + 2;                // [2]
   uint64_t* pv_done = p_full + 2;               // [2]
-  uint64_t* xch = pv_done + 2;                  // [2] row-max exchange between column halves
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xch + 2);
-  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+#ifdef SCREE_TRACE
+  const long long t_cta0 = clock64();
+#endif
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -175,12 +182,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_empty[b], 256);
-      mbar_init(&p_full[b], 256);
-      mbar_init(&pv_done[b], 1);
-      mbar_init(&xch[b], 256);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&s_full[x], 1);
+      mbar_init(&p_full[x], 128);
+      mbar_init(&pv_done[x], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -198,13 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
-    // Lane 0 streams Q and the K ring, lane 1 the V ring, each at its own pace.
     const int row0 = (int)seq_start;
     if (lane == 0) {
-      mbar_expect_tx(q_full, C::Q_BYTES);
+      mbar_expect_tx(q_full, (hasB ? 2 : 1) * C::Q_BYTES);
+      for (int x = 0; x < (hasB ? 2 : 1); ++x)
 #pragma unroll
-      for (int c = 0; c < C::NCHUNK; ++c)
-        tma_load_3d(smem + C::OFF_Q + c * BM * C::SWB, &tm_q, q_full, c * C::CHUNK, h, row0 + q0);
+        for (int c = 0; c < C::NCHUNK; ++c)
+          tma_load_3d(smem + C::OFF_Q + x * C::Q_BYTES + c * BM * C::SWB, &tm_q, q_full,
+                      c * C::CHUNK, h, row0 + q0 + x * BM);
       for (int j = 0; j < n_kv; ++j) {
         const int st = j % C::KSTAGES;
         if (j >= C::KSTAGES &&
@@ -232,94 +238,97 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      auto issue_pv = [&](int i) -> bool {
-        const int b2 = i & 1, st = i % C::VSTAGES;
-        if (!mbar_wait(&p_full[b2], (i >> 1) & 1, abort_flag, p.status, 2)) return false;
-        if (!mbar_wait(&v_full[st], (i / C::VSTAGES) & 1, abort_flag, p.status, 3)) return false;
-        tc_fence_after();
-        const uint32_t pb = sP;
-        const uint32_t vb = sV + st * C::KV_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16_ss(tmem + 256, p_desc(pb, kk), v_desc<D>(vb, kk), IDESC_O,
-                      (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&pv_done[b2]);
-        umma_commit(&v_empty[st]);
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 4);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int st = j % C::KSTAGES, b2 = j & 1;
-        if (!mbar_wait(&k_full[st], (j / C::KSTAGES) & 1, abort_flag, p.status, 5)) { ok = false; break; }
-        if (j >= 2 && !mbar_wait(&s_empty[b2], ((j - 2) >> 1) & 1, abort_flag, p.status, 6)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t kb = sK + st * C::KV_BYTES;
+      const int nX[2] = {nA, nB};
+      auto issue_s = [&](int x, int j) {
+        const uint32_t kb = sK + (j % C::KSTAGES) * C::KV_BYTES;
+        const uint32_t qb = sQ + x * C::Q_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16_ss(tmem + b2 * BN, kmajor_desc<D>(sQ, BM, kk), kmajor_desc<D>(kb, BN, kk),
-                      IDESC_S, kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[b2]);
-        umma_commit(&k_empty[st]);
-        if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
+          umma_f16_ss(tmem + C::COL_S + x * BN, kmajor_desc<D>(qb, BM, kk),
+                      kmajor_desc<D>(kb, BN, kk), IDESC_S, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[x]);
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t vb = sV + (j % C::VSTAGES) * C::KV_BYTES;
+        const uint32_t pt = tmem + C::COL_S + x * BN;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns per step
+          umma_f16_ts(tmem + C::COL_O + x * D, pt + kk * 8, v_desc<D>(vb, kk), IDESC_O,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[x]);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 4);
+      // Prologue: S_A(0), S_B(0).
+      if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, 5);
+      if (ok) {
+        tc_fence_after();
+        for (int x = 0; x < 2; ++x)
+          if (nX[x] > 0) issue_s(x, 0);
+        umma_commit(&k_empty[0]);
       }
-      if (ok && n_kv > 0) issue_pv(n_kv - 1);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int vst = j % C::VSTAGES;
+        const bool next_k = j + 1 < n_kv;
+        if (!(ok = mbar_wait(&v_full[vst], (j / C::VSTAGES) & 1, abort_flag, p.status, 3))) break;
+        if (next_k) {
+          const int kst = (j + 1) % C::KSTAGES;
+          if (!(ok = mbar_wait(&k_full[kst], ((j + 1) / C::KSTAGES) & 1, abort_flag, p.status, 5)))
+            break;
+        }
+        // Per tile X: O_X += P_X(j) V_j as soon as P_X(j) is ready, then
+        // S_X(j+1) into the same TMEM columns (issued after, so executed after).
+        for (int x = 0; x < 2; ++x) {
+          if (j < nX[x]) {
+            if (!(ok = mbar_wait(&p_full[x], j & 1, abort_flag, p.status, 2 + 4 * x))) break;
+            tc_fence_after();
+            issue_pv(x, j);
+            if (j + 1 < nX[x]) issue_s(x, j + 1);
+          }
+        }
+        if (!ok) break;
+        umma_commit(&v_empty[vst]);
+        if (next_k) umma_commit(&k_empty[(j + 1) % C::KSTAGES]);
+      }
     }
   } else {
     // ------------------------------------------------------------ softmax warps
-    // Warps w and w+4 share TMEM lanes 32*(w%4)..+31 (query rows); warp w < 4
-    // takes key columns [0,64) of each tile, warp w+4 columns [64,128).  The two
-    // halves exchange their row maxima once per tile (mbarrier xch, so the wait
-    // stays bounded) and their partial sums once at the end.
-    const int hf = warp >> 2;                 // column half
-    const int r = (warp & 3) * 32 + lane;     // query row within the tile == TMEM lane
+    const int x = warp >> 2;                  // query tile: 0 = A (warps 0-3), 1 = B (4-7)
+    const int r = (warp & 3) * 32 + lane;     // row within the tile == TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const int qi = q0 + r;                    // query index within the sequence
+    const uint32_t col_s = lane_base + C::COL_S + x * BN;
+    const uint32_t col_o = lane_base + C::COL_O + x * D;
+    const int qt0 = q0 + x * BM;              // first row of this tile
+    const int qi = qt0 + r;                   // query index within the sequence
+    const int nmine = x == 0 ? nA : nB;
     const float sl2 = p.scale_log2;
-    constexpr int HN = BN / 2;                // columns per half
     float m_used = -INFINITY;                 // running max, scaled log2 units
-    float l = 0.f;                            // partial sum over this half's columns
+    float l = 0.f;
     bool ok = true;
-    uint8_t* prow_base = smem + C::OFF_P + hf * BM * 128 + r * 128;
-    const int sw = r & 7;
-    for (int j = 0; j < n_kv; ++j) {
-      const int b2 = j & 1;
-      ok = mbar_wait(&s_full[b2], (j >> 1) & 1, abort_flag, p.status, 7);
+    for (int j = 0; j < nmine; ++j) {
+      ok = mbar_wait(&s_full[x], j & 1, abort_flag, p.status, 7);
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
-      float s[HN];
+      const int k0 = j * BN;
+      const bool need_mask = (k0 + BN > L) || (CAUSAL && k0 + BN - 1 > qt0);
+      const int lim = CAUSAL ? min(L - 1, qi) : (L - 1);  // last valid key
+      // Pass 1: row max over 32-column chunks (8 independent chains).
+      float mx8[8] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY,
+                      -INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < HN / 32; ++c)
-        tmem_ld32(lane_base + b2 * BN + hf * HN + c * 32,
-                  *reinterpret_cast<float(*)[32]>(&s[c * 32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_empty[b2]);
-
-      const int k0 = j * BN + hf * HN;
-      const bool need_mask = (j * BN + BN > L) || (CAUSAL && j * BN + BN - 1 > q0);
-      if (need_mask) {
-        const int lim = CAUSAL ? min(L - 1, qi) : (L - 1);  // last valid key
+      for (int c = 0; c < BN / 32; ++c) {
+        float s[32];
+        tmem_ld32(col_s + c * 32, s);
+        tmem_wait_ld();
+        if (need_mask) {
 #pragma unroll
-        for (int c = 0; c < HN; ++c)
-          if (k0 + c > lim) s[c] = -INFINITY;
+          for (int e = 0; e < 32; ++e)
+            if (k0 + c * 32 + e > lim) s[e] = -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], s[e]);
       }
-      // Row max: 8 independent chains, then the other half's value.
-      float mx8[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) mx8[a] = s[a];
-#pragma unroll
-      for (int c = 8; c < HN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      red[(b2 * 2 + hf) * BM + r] = mx;
-      mbar_arrive(&xch[b2]);
-      ok = mbar_wait(&xch[b2], (j >> 1) & 1, abort_flag, p.status, 10);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      mx = fmaxf(mx, red[(b2 * 2 + (hf ^ 1)) * BM + r]);
-      // Both halves now see the same max, so their lazy-rescale decisions agree.
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_cand = mx * sl2;
       float alpha = 1.f;
       bool need = false;
@@ -332,75 +341,70 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = ex2_approx(m_used - m_cand);
         m_used = m_cand;
       }
-      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
-      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < HN; ++c) {
-        s[c] = ex2_approx(fmaf(s[c], sl2, -m_eff));
-        rs8[c & 7] += s[c];
-      }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       if (j >= 1) {
-        ok = mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status, 8);
+        // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
+        // before P_X(j) overwrites the columns it read.  It already is in the
+        // common case: S_X(j) was issued after it and s_full covers both.
+        ok = mbar_wait(&pv_done[x], (j - 1) & 1, abort_flag, p.status, 8);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffff, need)) {
-          // O columns in 32-wide chunks; chunk c belongs to half c % 2.
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
-            if ((c & 1) != hf) continue;
             float o[32];
-            tmem_ld32(lane_base + 256 + c * 32, o);
+            tmem_ld32(col_o + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(lane_base + 256 + c * 32, o);
+            tmem_st32(col_o + c * 32, o);
           }
-          tmem_wait_st();
         }
       }
-      l = l * alpha + rs;
-      // This half's 64 keys are one 128-byte swizzled column block of P:
-      // 16-byte unit u of row r lives at unit position u ^ (r % 8).
-      uint8_t* prow = prow_base;
+      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // Pass 2: re-read each chunk, exponentiate, accumulate, pack to 16 bits.
+      uint32_t pk[BN / 2];
 #pragma unroll
-      for (int u = 0; u < HN / 8; ++u) {
-        uint4 w;
-        w.x = Pk2<T>::pack(s[u * 8 + 0], s[u * 8 + 1]);
-        w.y = Pk2<T>::pack(s[u * 8 + 2], s[u * 8 + 3]);
-        w.z = Pk2<T>::pack(s[u * 8 + 4], s[u * 8 + 5]);
-        w.w = Pk2<T>::pack(s[u * 8 + 6], s[u * 8 + 7]);
-        *reinterpret_cast<uint4*>(prow + ((u ^ sw) << 4)) = w;
+      for (int c = 0; c < BN / 32; ++c) {
+        float s[32];
+        tmem_ld32(col_s + c * 32, s);
+        tmem_wait_ld();
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (k0 + c * 32 + e > lim) s[e] = -INFINITY;
+        }
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float e0 = ex2_approx(fmaf(s[e], sl2, -m_eff));
+          const float e1 = ex2_approx(fmaf(s[e + 1], sl2, -m_eff));
+          rs8[e & 7] += e0;
+          rs8[(e + 1) & 7] += e1;
+          pk[c * 16 + e / 2] = Pk2<T>::pack(e0, e1);
+        }
       }
-      fence_proxy_async_smem();
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      l = l * alpha + rs;
+      tmem_st32u(col_s, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_st32u(col_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[b2]);
+      mbar_arrive(&p_full[x]);
     }
     // ------------------------------------------------------------ epilogue
-    if (ok && n_kv > 0) {
-      ok = mbar_wait(&pv_done[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, abort_flag, p.status, 9);
+    if (ok && nmine > 0) {
+      ok = mbar_wait(&pv_done[x], (nmine - 1) & 1, abort_flag, p.status, 9);
       ok = __all_sync(0xffffffff, ok);
     }
-    if (ok && n_kv > 0) {
-      // Total row sum: exchange the partial sums through the exchange buffer of
-      // the parity the last tile did not use (its readers have moved on).
-      const int pb = n_kv & 1;
-      red[(pb * 2 + hf) * BM + r] = l;
-      mbar_arrive(&xch[pb]);
-      ok = mbar_wait(&xch[pb], (n_kv >> 1) & 1, abort_flag, p.status, 11);
-      ok = __all_sync(0xffffffff, ok);
-      if (ok) l += red[(pb * 2 + (hf ^ 1)) * BM + r];
-    }
-    if (ok && n_kv > 0) {
+    if (ok && nmine > 0) {
       tc_fence_after();
       const bool row_ok = qi < L;
       const float inv_l = 1.0f / l;
       T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
-        if ((c & 1) != hf) continue;
         float o[32];
-        tmem_ld32(lane_base + 256 + c * 32, o);
+        tmem_ld32(col_o + c * 32, o);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
@@ -414,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (hf == 0 && row_ok && p.lse != nullptr)
+      if (row_ok && p.lse != nullptr)
         p.lse[(seq_start + qi) * p.H + h] = (m_used + log2f(l)) * 0.69314718055994531f;
     }
   }
@@ -422,6 +426,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+#ifdef SCREE_TRACE
+  if (threadIdx.x == 0) {
+    atomicAdd(&g_fwd_trace[30], (unsigned long long)(clock64() - t_cta0));
+    atomicAdd(&g_fwd_trace[31], (unsigned long long)n_kv);
+  }
+#endif
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc<512>(tmem);
@@ -487,7 +497,7 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
   if ((rc = make_thd_map(&tq, q, T, H, D, q_rs, q_hs, swb / 2, BM, swb, bf16))) return rc;
   if ((rc = make_thd_map(&tk, k, T, H, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
   if ((rc = make_thd_map(&tv, v, T, H, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
-  if ((rc = launch_build_schedule(offsets, offs_is_i64, B, BM, (int)H, workspace, s))) return rc;
+  if ((rc = launch_build_schedule(offsets, offs_is_i64, B, ROWS, (int)H, workspace, s))) return rc;
   FwdParams p;
   p.offs = offsets;
   p.is64 = offs_is_i64;
@@ -501,7 +511,7 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
   p.o_rs = o_rs;
   p.o_hs = o_hs;
   p.lse = lse;
-  const int64_t grid = max_tiles(B, T, BM) * H;
+  const int64_t grid = max_tiles(B, T, ROWS) * H;
   SCREE_CHECK_ARG(grid < (1ll << 31), "attn_fwd: grid too large");
 #define SCREE_FWD_CASE(DD)                                                              \
   if (D == DD) {                                                                        \
@@ -579,3 +589,15 @@ extern "C" int scree_attn_fwd_noalloc(const void* q, const void* k, const void* 
                         H, D, dtype, causal, scale, max_seqlen, o, o_rs, o_hs, lse,
                         scratch_ptr[dev], kNoAllocScratchBytes, stream);
 }
+
+#ifdef SCREE_TRACE
+extern "C" int scree_fwd_trace_read(unsigned long long* out32, int reset) {
+  SCREE_CUDA_TRY(cudaDeviceSynchronize());
+  SCREE_CUDA_TRY(cudaMemcpyFromSymbol(out32, g_fwd_trace, sizeof(unsigned long long) * 32));
+  if (reset) {
+    unsigned long long z[32] = {0};
+    SCREE_CUDA_TRY(cudaMemcpyToSymbol(g_fwd_trace, z, sizeof(z)));
+  }
+  return SCREE_OK;
+}
+#endif
