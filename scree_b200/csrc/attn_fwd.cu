@@ -43,7 +43,12 @@ namespace {
 constexpr int BM = 128;      // rows per query tile
 constexpr int ROWS = 2 * BM; // query rows per CTA (tiles A and B)
 constexpr int BN = 128;      // keys per K/V tile
-constexpr int kThreads = 320;  // 8 softmax warps, TMA warp, MMA warp
+// 8 softmax warps (warpgroups 0, 1), then warpgroup 2: TMA warp, MMA warp and two
+// idle warps.  Launched at 168 registers per thread (65,536 / 384); the
+// softmax warpgroups grow to 224 and warpgroup 2 shrinks to 56:
+// 256 x 224 + 128 x 56 = 64,512 = 384 x 168.
+constexpr int kThreads = 384;
+constexpr int kRegsSoftmax = 224, kRegsOther = 56;
 
 template <int D>
 struct FwdCfg {
@@ -200,9 +205,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
+    regs_dec<kRegsOther>();
     const int row0 = (int)seq_start;
     if (lane == 0) {
       mbar_expect_tx(q_full, (hasB ? 2 : 1) * C::Q_BYTES);
@@ -237,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
+    regs_dec<kRegsOther>();
     if (elect_one()) {
       const int nX[2] = {nA, nB};
       auto issue_s = [&](int x, int j) {
@@ -290,8 +296,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (next_k) umma_commit(&k_empty[(j + 1) % C::KSTAGES]);
       }
     }
+  } else if (warp >= 10) {
+    regs_dec<kRegsOther>();  // idle: only completes warpgroup 2's register release
   } else {
     // ------------------------------------------------------------ softmax warps
+    regs_inc<kRegsSoftmax>();
     const int x = warp >> 2;                  // query tile: 0 = A (warps 0-3), 1 = B (4-7)
     const int r = (warp & 3) * 32 + lane;     // row within the tile == TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
@@ -308,25 +317,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(&s_full[x], j & 1, abort_flag, p.status, 7);
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
+      // One TMEM load of the whole 128-column row (a single wait::ld).
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_ld32(col_s + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      tmem_wait_ld();
       const int k0 = j * BN;
       const bool need_mask = (k0 + BN > L) || (CAUSAL && k0 + BN - 1 > qt0);
-      const int lim = CAUSAL ? min(L - 1, qi) : (L - 1);  // last valid key
-      // Pass 1: row max over 32-column chunks (8 independent chains).
-      float mx8[8] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY,
-                      -INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (need_mask) {
+        const int lim = CAUSAL ? min(L - 1, qi) : (L - 1);  // last valid key
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float s[32];
-        tmem_ld32(col_s + c * 32, s);
-        tmem_wait_ld();
-        if (need_mask) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (k0 + c * 32 + e > lim) s[e] = -INFINITY;
-        }
-#pragma unroll
-        for (int e = 0; e < 32; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], s[e]);
+        for (int c = 0; c < BN; ++c)
+          if (k0 + c > lim) s[c] = -INFINITY;
       }
+      float mx8[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) mx8[a] = s[a];
+#pragma unroll
+      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
       const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                              fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float m_cand = mx * sl2;
@@ -341,6 +350,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         alpha = ex2_approx(m_used - m_cand);
         m_used = m_cand;
       }
+      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+      // Exponentiate and pack: each pair of S values dies as its packed word appears.
+      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int c = 0; c < BN; c += 2) {
+        const float e0 = ex2_approx(fmaf(s[c], sl2, -m_eff));
+        const float e1 = ex2_approx(fmaf(s[c + 1], sl2, -m_eff));
+        rs8[c & 7] += e0;
+        rs8[(c + 1) & 7] += e1;
+        pk[c / 2] = Pk2<T>::pack(e0, e1);
+      }
+      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       if (j >= 1) {
         // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
         // before P_X(j) overwrites the columns it read.  It already is in the
@@ -360,30 +382,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
-      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      // Pass 2: re-read each chunk, exponentiate, accumulate, pack to 16 bits.
-      uint32_t pk[BN / 2];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        float s[32];
-        tmem_ld32(col_s + c * 32, s);
-        tmem_wait_ld();
-        if (need_mask) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            if (k0 + c * 32 + e > lim) s[e] = -INFINITY;
-        }
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float e0 = ex2_approx(fmaf(s[e], sl2, -m_eff));
-          const float e1 = ex2_approx(fmaf(s[e + 1], sl2, -m_eff));
-          rs8[e & 7] += e0;
-          rs8[(e + 1) & 7] += e1;
-          pk[c * 16 + e / 2] = Pk2<T>::pack(e0, e1);
-        }
-      }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
       l = l * alpha + rs;
       tmem_st32u(col_s, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
       tmem_st32u(col_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));

@@ -266,6 +266,19 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
+// ---------------------------------------------------------------- register split
+// Per-warpgroup register reallocation; every warp of a warpgroup executes the
+// same call.  The increases and decreases of a kernel must add up to no more
+// than the registers the block was launched with.
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ---------------------------------------------------------------- math helpers
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
