@@ -22,13 +22,25 @@
 //   D <= 64: BQ = 128 and dQ_i = dS K (M = 128 queries, N = D).
 // TMEM columns: S^T [0,BQ), dP^T [BQ,2BQ), dV [2BQ,2BQ+D), dK [.., +D), dQ [.., +BQ or D).
 #include <algorithm>
+#ifdef SCREE_TRACE
+// Profiling build only: per-site wait cycles (lane 0 of each waiting warp),
+// [62] = CTA lifetime cycles, [63] = query tiles processed.
+static __device__ unsigned long long g_bwd_trace[64];
+#define SCREE_TRACE_ADD(site, cyc) \
+  do { if ((threadIdx.x & 31) == 0) atomicAdd(&g_bwd_trace[(site) & 63], (unsigned long long)(cyc)); } while (0)
+#endif
 #include "attn_common.cuh"
 
 namespace scree {
 namespace {
 
 constexpr int BN = 128;  // keys per CTA
-constexpr int kThreads = 320;
+// Warpgroup 0: P^T / dS^T (softmax) warps; warpgroup 1: dQ reduction warps;
+// warpgroup 2: TMA warp, MMA warp, two idle warps.  Launched at 168 registers
+// per thread (65,536 / 384); warpgroup 0 grows to 240, warpgroup 2 shrinks to 80:
+// 128 x 240 + 128 x 168 + 128 x 80 = 62,464 <= 384 x 168 = 64,512.
+constexpr int kThreads = 384;
+constexpr int kRegsSoftmax = 240, kRegsOther = 80;
 
 template <int D>
 struct BwdCfg {
@@ -47,13 +59,15 @@ struct BwdCfg {
   static constexpr int OFF_Q = OFF_V + KV_BYTES;
   static constexpr int OFF_DO = OFF_Q + STAGES * QT_BYTES;
   static constexpr int OFF_PT = OFF_DO + STAGES * QT_BYTES;
-  static constexpr int OFF_DS = OFF_PT + PT_BYTES;
+  static constexpr int OFF_DS = OFF_PT;  // P^T lives in TMEM only (no smem buffer)
   static constexpr int OFF_LD = OFF_DS + PT_BYTES;          // lse2 / delta [2][2][BQ] fp32
   static constexpr int OFF_DQ = OFF_LD + 2 * 2 * BQ * 4;    // DQT: dQ tile [BQ][D] fp32
   static constexpr int DQ_BYTES = DQT ? BQ * D * 4 : 0;
   static constexpr int OFF_BAR = OFF_DQ + DQ_BYTES;
   // At least 120 KB so two CTAs (each holding all 512 TMEM columns) never share an SM.
-  static constexpr int SMEM_RAW = OFF_BAR + 512 + 1024;
+  static constexpr int OFF_END = OFF_BAR + 512;
+  // 1 KB of alignment slack when it fits; the kernel checks the real alignment.
+  static constexpr int SMEM_RAW = OFF_END + 1024 <= 232448 ? OFF_END + 1024 : OFF_END;
   static constexpr int SMEM = SMEM_RAW > 120 * 1024 ? SMEM_RAW : 120 * 1024;
   static constexpr int COL_S = 0, COL_DP = BQ, COL_DV = 2 * BQ, COL_DK = 2 * BQ + D,
                        COL_DQ = 2 * BQ + 2 * D;
@@ -177,6 +191,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
+  {
+    uint32_t dyn;
+    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    if ((uint32_t)(smem - smem_raw) + (uint32_t)C::OFF_END > dyn) {
+      if (threadIdx.x == 0) record_device_error(p.status, SCREE_DEVERR_BAD_INPUT, 91);
+      return;
+    }
+  }
   const uint32_t sK = smem_u32(smem + C::OFF_K), sV = smem_u32(smem + C::OFF_V);
   const uint32_t sQ = smem_u32(smem + C::OFF_Q), sDO = smem_u32(smem + C::OFF_DO);
   const uint32_t sPT = smem_u32(smem + C::OFF_PT), sDS = smem_u32(smem + C::OFF_DS);
@@ -198,6 +220,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
+#ifdef SCREE_TRACE
+  const long long t_cta0 = clock64();
+#endif
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -231,6 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
+    regs_dec<kRegsOther>();
     if (elect_one()) {
       mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
 #pragma unroll
@@ -258,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
+    regs_dec<kRegsOther>();
     if (elect_one()) {
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 22) && mbar_wait(&q_full[0], 0, abort_flag, p.status, 23);
       auto issue_s_dp = [&](int it, bool s_part) {
@@ -291,8 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          umma_f16_ss(tmem + C::COL_DV, pt_kmaj(sPT, kk), mnmaj<D>(ob, BQ, kk), ID_ACC,
-                      (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + kk * 8, mnmaj<D>(ob, BQ, kk), ID_ACC,
+                      (it > 0 || kk > 0) ? 1u : 0u);  // A = P^T from TMEM (16 q = 8 columns)
         umma_commit(p_free);
         // S^T for the next query tile overlaps the softmax warps' dS work.
         const bool more = it + 1 < n_it;
@@ -302,16 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           issue_s_dp(it + 1, true);
         }
-        // dS_i published: the softmax warps are done reading dP_i, so dP_{i+1}
-        // goes first and their next dS phase waits on one GEMM, not three.
+        // dS_i published (in TMEM over dP^T_i's columns and in smem).  dK first:
+        // it reads dS^T from those TMEM columns, so dP_{i+1} (which overwrites
+        // them) is issued after it; the dQ GEMM follows.
         if (!(ok = mbar_wait(ds_full, it & 1, abort_flag, p.status, 26))) break;
         tc_fence_after();
-        if (more) issue_s_dp(it + 1, false);
-        // dK += dS^T Q_i ; dQ_i
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          umma_f16_ss(tmem + C::COL_DK, pt_kmaj(sDS, kk), mnmaj<D>(qb, BQ, kk), ID_ACC,
+          umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + kk * 8, mnmaj<D>(qb, BQ, kk), ID_ACC,
                       (it > 0 || kk > 0) ? 1u : 0u);
+        if (more) issue_s_dp(it + 1, false);
         if (it > 0 && !(ok = mbar_wait(dq_empty, (it - 1) & 1, abort_flag, p.status, 27))) break;
         tc_fence_after();
 #pragma unroll
@@ -329,8 +356,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma_commit(acc_done);
     }
+  } else if (warp >= 10) {
+    regs_dec<kRegsOther>();  // idle: only completes warpgroup 2's register release
   } else if (warp < 4) {
     // ------------------------------------------------------------ P^T / dS^T
+    regs_inc<kRegsSoftmax>();
     const int kr = threadIdx.x;  // key row within the tile == TMEM lane
     const int kidx = k0 + kr;
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
@@ -377,22 +407,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BQ / 32; ++c)
         tmem_ld32(lane_base + C::COL_S + c * 32, *reinterpret_cast<float(*)[32]>(&pr[c * 32]));
       tmem_wait_ld();
+      uint32_t pk[BQ / 2];
 #pragma unroll
-      for (int c = 0; c < BQ; ++c) {
-        float x = ex2_approx(fmaf(pr[c], sl2, -lse_s[c]));
-        if (need_mask) {
-          const int q = q0 + c;
-          const bool valid = key_ok && q < L && (!CAUSAL || q >= kidx);
-          x = valid ? x : 0.f;
+      for (int c4 = 0; c4 < BQ / 4; ++c4) {
+        const float4 l4 = reinterpret_cast<const float4*>(lse_s)[c4];  // one LDS.128
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int c = c4 * 4 + e;
+          float xv = ex2_approx(fmaf(pr[c], sl2, -lv[e]));
+          if (need_mask) {
+            const int q = q0 + c;
+            const bool valid = key_ok && q < L && (!CAUSAL || q >= kidx);
+            xv = valid ? xv : 0.f;
+          }
+          pr[c] = xv;
         }
-        pr[c] = x;
+        pk[c4 * 2] = Pk2b<T>::pack(pr[c4 * 4], pr[c4 * 4 + 1]);
+        pk[c4 * 2 + 1] = Pk2b<T>::pack(pr[c4 * 4 + 2], pr[c4 * 4 + 3]);
       }
-      if (it > 0) {
+      if (it > 0) {  // dV_{i-1} read P^T_{i-1} from these columns
         ok = mbar_wait(p_free, (it - 1) & 1, abort_flag, p.status, 29);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       }
-      write_row_sw128<T, BQ>(smem + C::OFF_PT, kr, pr);
-      fence_proxy_async_smem();
+      // P^T (16-bit, two per column) over the first BQ/2 columns of S^T.
+#pragma unroll
+      for (int c = 0; c < BQ / 64; ++c)
+        tmem_st32u(lane_base + C::COL_S + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[c * 32]));
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
       // ---- dS^T = P^T * (dP^T - Delta)
@@ -405,13 +447,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(lane_base + C::COL_DP + c * 32, dp);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) pr[c * 32 + e] *= (dp[e] - del_s[c * 32 + e]);
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 d4 = reinterpret_cast<const float4*>(del_s)[c * 8 + e4];
+          pr[c * 32 + e4 * 4 + 0] *= (dp[e4 * 4 + 0] - d4.x);
+          pr[c * 32 + e4 * 4 + 1] *= (dp[e4 * 4 + 1] - d4.y);
+          pr[c * 32 + e4 * 4 + 2] *= (dp[e4 * 4 + 2] - d4.z);
+          pr[c * 32 + e4 * 4 + 3] *= (dp[e4 * 4 + 3] - d4.w);
+        }
       }
+#pragma unroll
+      for (int c = 0; c < BQ / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
       if (it > 0) {
         ok = mbar_wait(ds_free, (it - 1) & 1, abort_flag, p.status, 31);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       }
+      // dS^T: into TMEM over dP^T's first columns (A operand of dK) and into
+      // smem (B operand of the dQ GEMM).
+#pragma unroll
+      for (int c = 0; c < BQ / 64; ++c)
+        tmem_st32u(lane_base + C::COL_DP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[c * 32]));
       write_row_sw128<T, BQ>(smem + C::OFF_DS, kr, pr);
+      tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
@@ -506,6 +562,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+#ifdef SCREE_TRACE
+  if (threadIdx.x == 0) {
+    atomicAdd(&g_bwd_trace[62], (unsigned long long)(clock64() - t_cta0));
+    atomicAdd(&g_bwd_trace[63], (unsigned long long)n_it);
+  }
+#endif
   if (warp == 9) {
     tc_fence_after();
     tmem_dealloc<C::TMEM_COLS>(tmem);
@@ -703,3 +765,15 @@ extern "C" int scree_attn_bwd(const void* dout, const void* q, const void* k, co
   return run_bwd_typed<__half>(dout, q, k, v, o, lse, offsets, offs_is_i64, B, T, H, D, causal,
                                scale, dq, dk, dv, ws, L, s);
 }
+
+#ifdef SCREE_TRACE
+extern "C" int scree_bwd_trace_read(unsigned long long* out64, int reset) {
+  SCREE_CUDA_TRY(cudaDeviceSynchronize());
+  SCREE_CUDA_TRY(cudaMemcpyFromSymbol(out64, g_bwd_trace, sizeof(unsigned long long) * 64));
+  if (reset) {
+    unsigned long long z[64] = {0};
+    SCREE_CUDA_TRY(cudaMemcpyToSymbol(g_bwd_trace, z, sizeof(z)));
+  }
+  return SCREE_OK;
+}
+#endif
