@@ -251,6 +251,100 @@ def workload_config(args, lengths, H, D, causal, world):
     }
 
 
+# ----------------------------------------------------------------------------- norms suite
+def run_norm_suite(args):
+    """cfg3: 64 sequences, lengths lognormal(ln 256, 0.6) (T = 19,794), hidden 4096
+    bf16.  Each op is timed per launch with CUDA events; a 256 MB buffer is
+    written between launches to flush the 126 MB L2.  Bandwidth = algorithmic
+    bytes (reads + writes the op must do) / time, against MEASURED_PEAKS hbm_gbs."""
+    import torch
+
+    import scree_b200 as scree
+    from scree_b200 import _lib, workloads
+    from scree_b200.kernels import native
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lengths = workloads.cfg3_lengths()
+    T, C, b = sum(lengths), 4096, 2
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn((T, C), device=dev, generator=g).to(torch.bfloat16)
+    dy = torch.randn((T, C), device=dev, generator=g).to(torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(C, device=dev, generator=g))
+    bias = 0.02 * torch.randn(C, device=dev, generator=g)
+    offs = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device=dev)
+    arr = scree.from_cu_seqlens(x, offs)
+    rows = scree.unpack(arr)
+    Lmax = max(lengths)
+    padded, mask = scree.to_padded(arr)
+    _, rstd = native._rmsnorm_fwd(x, w, 1e-5, True)
+    _, mean, rstd_l = native._layernorm_fwd(x, w, bias, 1e-5, True)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    B = len(lengths)
+    ops = {
+        "rmsnorm_fwd": (lambda: native.varlen_rmsnorm_triton(x, w, 1e-5), 2 * T * C * b + 4 * C),
+        "rmsnorm_bwd": (lambda: native.varlen_rmsnorm_backward(dy, x, w, rstd), 3 * T * C * b + 4 * T + 4 * C),
+        "layernorm_fwd": (lambda: native.varlen_layernorm_triton(x, w, bias, 1e-5), 2 * T * C * b + 8 * C),
+        "layernorm_bwd": (lambda: native.varlen_layernorm_backward(dy, x, w, bias, mean, rstd_l), 3 * T * C * b + 8 * T + 8 * C),
+        "pack": (lambda: scree.pack(rows), 2 * T * C * b + 4 * (B + 1)),
+        "to_padded": (lambda: scree.to_padded(arr), T * C * b + B * Lmax * C * b + B * Lmax),
+        "from_padded": (lambda: scree.from_padded(padded, mask), B * Lmax + 2 * T * C * b),
+    }
+    peaks, kind = load_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    res = {}
+    for name, (fn, nbytes) in ops.items():
+        for _ in range(max(3, args.warmup)):
+            fn()
+        # Kernel-only time from the library's CUDA-event hooks around each
+        # launch; the 256 MB flush is written before every launch.
+        kind_ = _lib.PROF_NORM_FWD if name.endswith("_fwd") else (_lib.PROF_NORM_BWD if name.endswith("_bwd") else _lib.PROF_GATHER)
+        times = []
+        _lib.profile_read(kind_)
+        _lib.profile_enable(True)
+        for _ in range(args.steps):
+            flush.fill_(1)
+            fn()
+            torch.cuda.synchronize()
+            tms, nl = _lib.profile_read(kind_)
+            times.append(tms / max(nl, 1) * max(nl, 1))  # all launches of one call
+        _lib.profile_enable(False)
+        ms = statistics.median(times)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"ms": ms, "algorithmic_bytes": int(nbytes), "gb_s": gbs, "frac": gbs / hbm}
+    assert _lib.device_status() == 0
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+
+        xn = x.float().cpu().numpy()
+        wn = w.cpu().numpy()
+        oracle.rmsnorm_fwd(xn, wn, 1e-5, dtype=np.float32)
+        t0 = time.perf_counter()
+        oracle.rmsnorm_fwd(xn, wn, 1e-5, dtype=np.float32)
+        t_cpu = time.perf_counter() - t0
+        cpu = {"value": 2 * T * C * b / t_cpu / 1e9, "unit": "GB/s", "cores": len(os.sched_getaffinity(0)),
+               "kind": "port", "sample": f"rmsnorm_fwd on the full cfg3 batch (fp32 numpy oracle), {t_cpu:.3f} s"}
+    line = {
+        "metric": "varlen norms / gathers HBM GB/s (cfg3)",
+        "value": res["rmsnorm_fwd"]["gb_s"],
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": max(3, args.warmup),
+        "higher_is_better": True,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"cfg3: 64 seqs lognormal(ln 256, 0.6) seed 0, T={T}, hidden {C} bf16",
+                   "l2": "256 MB buffer written before every timed call", "timing": "kernel time from CUDA events around each launch inside libscree_b200 (all launches of the call summed)"},
+        "ops": res,
+        "hbm_peak_gbs": hbm,
+        "peak_source": kind,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -263,11 +357,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--non-causal", action="store_true")
+    ap.add_argument("--suite", choices=["attention", "norms"], default="attention",
+                    help="norms: cfg3 RMSNorm/LayerNorm fwd+bwd and pack/unpack/to_padded/from_padded")
     ap.add_argument("--max-seqs", type=int, default=0, help="keep only the first N sequences (small profiling case)")
     args = ap.parse_args()
 
     from scree_b200 import workloads
 
+    if args.suite == "norms":
+        run_norm_suite(args)
+        return
     cfg = workloads.attn_config(args.config)
     lengths = list(cfg.lengths)
     if args.max_seqs:

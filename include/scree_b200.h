@@ -49,7 +49,8 @@ long long scree_launch_count(void);
 /* Per-kernel timing for benchmarks: when enabled, each main kernel launch is
  * bracketed by CUDA events on its stream.  scree_profile_read() waits for the
  * recorded events, returns the summed milliseconds and launch count of one
- * kernel kind (0 attention fwd, 1 attention bwd, 2 norm fwd, 3 norm bwd) and
+ * kernel kind (0 attention fwd, 1 attention bwd, 2 norm fwd, 3 norm bwd,
+ * 4 gathers) and
  * clears them.  Neither call has a reference counterpart. */
 int scree_profile_enable(int on);
 int scree_profile_read(int kernel, double* total_ms, long long* launches);
@@ -147,10 +148,12 @@ int scree_layernorm_bwd(const void* dy, const void* x, const void* weight, int w
  * src_ptrs: device array of B source pointers; offsets: device (B+1,) row
  * offsets (int64 when offs_is_i64); row_bytes = bytes of one row (prod of the
  * feature dims x element size).  src_align: a power of two dividing every
- * source address (e.g. 16 when all are 16-byte aligned).  dst: (T, ...)
+ * source address (e.g. 16 when all are 16-byte aligned).  max_rows: the longest
+ * sequence (sizes the grid; <= 0 means unknown and T is used).  dst: (T, ...)
  * contiguous. */
 int scree_pack(const void* const* src_ptrs, const void* offsets, int offs_is_i64, int64_t B,
-               int64_t T, int64_t row_bytes, int64_t src_align, void* dst, void* stream);
+               int64_t T, int64_t max_rows, int64_t row_bytes, int64_t src_align, void* dst,
+               void* stream);
 
 /* to_padded: (T, ...) packed -> (B, max_len, ...) padded + (B, max_len) mask.
  * Replaces: scree/_core.py:161-250 to_padded (torch branch :224-250).

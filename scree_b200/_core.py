@@ -190,7 +190,8 @@ def _pack_values(arrays, host):
     if T and row_bytes:
         with torch.cuda.device(dev):
             rc = _lib.load().scree_pack(
-                ptrs_d.data_ptr(), offsets.data_ptr(), 0, B, T, row_bytes, align,
+                ptrs_d.data_ptr(), offsets.data_ptr(), 0, B, T,
+                max(host[i + 1] - host[i] for i in range(B)), row_bytes, align,
                 values.data_ptr(), _lib.stream_ptr(dev),
             )
         _lib.check(rc, "scree_pack")

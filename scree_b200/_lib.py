@@ -52,7 +52,7 @@ _SIGNATURES = {
     "scree_rmsnorm_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _L, _L, _I, _P, _S, _P]),
     "scree_layernorm_fwd": (_I, [_P, _L, _P, _P, _I, _P, _L, _P, _P, _L, _L, _I, _F, _P]),
     "scree_layernorm_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _L, _L, _I, _P, _S, _P]),
-    "scree_pack": (_I, [_P, _P, _I, _L, _L, _L, _L, _P, _P]),
+    "scree_pack": (_I, [_P, _P, _I, _L, _L, _L, _L, _L, _P, _P]),
     "scree_to_padded": (_I, [_P, _P, _I, _L, _L, _L, _L, _P, _I, _P, _P, _P]),
     "scree_padded_lengths": (_I, [_P, _L, _L, _P, _P]),
     "scree_from_padded": (_I, [_P, _P, _L, _L, _L, _L, _P, _P]),
@@ -114,7 +114,7 @@ def device_status(reset: bool = True) -> int:
     return v.value
 
 
-PROF_ATTN_FWD, PROF_ATTN_BWD, PROF_NORM_FWD, PROF_NORM_BWD = 0, 1, 2, 3
+PROF_ATTN_FWD, PROF_ATTN_BWD, PROF_NORM_FWD, PROF_NORM_BWD, PROF_GATHER = 0, 1, 2, 3, 4
 
 
 def profile_enable(on: bool) -> None:

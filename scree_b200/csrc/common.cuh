@@ -56,7 +56,7 @@ void count_launch();
 
 // Optional per-kernel timing (scree_profile_enable): CUDA events recorded on the
 // launch stream around the main kernel of an entry point.
-enum ProfKernel : int { PROF_ATTN_FWD = 0, PROF_ATTN_BWD = 1, PROF_NORM_FWD = 2, PROF_NORM_BWD = 3, PROF_N = 4 };
+enum ProfKernel : int { PROF_ATTN_FWD = 0, PROF_ATTN_BWD = 1, PROF_NORM_FWD = 2, PROF_NORM_BWD = 3, PROF_GATHER = 4, PROF_N = 5 };
 struct ProfScope {
   int kernel;
   cudaStream_t stream;

@@ -28,71 +28,63 @@ template <> struct Vec<4> { using T = uint32_t; };
 template <> struct Vec<2> { using T = uint16_t; };
 template <> struct Vec<1> { using T = uint8_t; };
 
-int grid_for(int64_t work_items) {
-  int64_t per_sm = 8;  // 8 x 256 threads resident per SM
-  int64_t g = (work_items + kThreads - 1) / kThreads;
-  return (int)std::max<int64_t>(1, std::min<int64_t>(g, (int64_t)num_sms() * per_sm));
-}
-
-// Binary search: largest b with offsets[b] <= row, over b in [0, B).
-__device__ __forceinline__ int64_t find_seq(const void* offs, int is64, int64_t B, int64_t row) {
-  int64_t lo = 0, hi = B - 1;
-  while (lo < hi) {
-    int64_t mid = (lo + hi + 1) >> 1;
-    if (load_offset(offs, is64, mid) <= row) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
+// All three gathers use a 2-D grid: blockIdx.y walks sequences (padded rows),
+// blockIdx.x a chunk of `rows_per_cta` rows of that sequence; threads stride
+// over the W-byte vectors of those rows.  No per-element search and no 64-bit
+// division: one 32-bit division by the vectors-per-row count per element.
 
 // ---------------------------------------------------------------- pack
-// Output vector v (W bytes) lies in row t = v*W / row_bytes of sequence b; it is
-// copied from src_ptrs[b] at the same byte position relative to the sequence.
 template <int W>
-__global__ void pack_kernel(const void* const* __restrict__ src, const void* offs, int is64,
-                            int64_t B, int64_t row_bytes, int64_t nvec, void* __restrict__ dst) {
+__global__ void __launch_bounds__(kThreads) pack_kernel(
+    const void* const* __restrict__ src, const void* offs, int is64, int64_t B,
+    int64_t row_bytes, int rows_per_cta, void* __restrict__ dst) {
   using V = typename Vec<W>::T;
-  const int64_t vec_per_row = row_bytes / W;
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
-       v += (int64_t)gridDim.x * blockDim.x) {
-    int64_t row = v / vec_per_row;
-    int64_t b = find_seq(offs, is64, B, row);
-    int64_t rel = v - load_offset(offs, is64, b) * vec_per_row;
-    reinterpret_cast<V*>(dst)[v] = reinterpret_cast<const V*>(src[b])[rel];
+  const uint32_t vpr = (uint32_t)(row_bytes / W);
+  for (int64_t b = blockIdx.y; b < B; b += gridDim.y) {
+    const int64_t s = load_offset(offs, is64, b);
+    const int64_t len = load_offset(offs, is64, b + 1) - s;
+    const int64_t j0 = (int64_t)blockIdx.x * rows_per_cta;
+    if (j0 >= len) continue;
+    const uint32_t nrows = (uint32_t)(rows_per_cta < len - j0 ? rows_per_cta : len - j0);
+    const V* __restrict__ sp = reinterpret_cast<const V*>(src[b]) + j0 * vpr;
+    V* __restrict__ dp = reinterpret_cast<V*>(dst) + (s + j0) * vpr;
+    const uint32_t n = nrows * vpr;
+    for (uint32_t v = threadIdx.x; v < n; v += blockDim.x) dp[v] = sp[v];
   }
 }
 
 // ---------------------------------------------------------------- to_padded
 template <int W>
-__global__ void to_padded_kernel(const void* __restrict__ values, const void* offs, int is64,
-                                 int64_t B, int64_t max_len, int64_t row_bytes, uint4 fill16,
-                                 int side_left, void* __restrict__ padded,
-                                 uint8_t* __restrict__ mask) {
+__global__ void __launch_bounds__(kThreads) to_padded_kernel(
+    const void* __restrict__ values, const void* offs, int is64, int64_t B, int64_t max_len,
+    int64_t row_bytes, int rows_per_cta, uint4 fill16, int side_left, void* __restrict__ padded,
+    uint8_t* __restrict__ mask) {
   using V = typename Vec<W>::T;
-  const int64_t vec_per_row = row_bytes / W;
-  const int64_t per_seq = max_len * vec_per_row;
-  const int64_t nvec = B * per_seq;
   V fill;
   memcpy(&fill, &fill16, sizeof(V));
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  for (int64_t v = tid; v < nvec; v += stride) {
-    int64_t b = v / per_seq;
-    int64_t j = (v - b * per_seq) / vec_per_row;
-    int64_t inner = v - b * per_seq - j * vec_per_row;
-    int64_t s = load_offset(offs, is64, b), e = load_offset(offs, is64, b + 1);
-    int64_t len = e - s;
-    int64_t src_row = side_left ? j - (max_len - len) : j;
-    V out = fill;
-    if (src_row >= 0 && src_row < len)
-      out = reinterpret_cast<const V*>(values)[(s + src_row) * vec_per_row + inner];
-    reinterpret_cast<V*>(padded)[v] = out;
-  }
-  if (mask != nullptr) {
-    for (int64_t i = tid; i < B * max_len; i += stride) {
-      int64_t b = i / max_len, j = i - b * max_len;
-      int64_t len = load_offset(offs, is64, b + 1) - load_offset(offs, is64, b);
-      mask[i] = side_left ? (j >= max_len - len) : (j < len);
+  const uint32_t vpr = (uint32_t)(row_bytes / W);
+  for (int64_t b = blockIdx.y; b < B; b += gridDim.y) {
+    const int64_t s = load_offset(offs, is64, b);
+    const int64_t len = load_offset(offs, is64, b + 1) - s;
+    const int64_t j0 = (int64_t)blockIdx.x * rows_per_cta;
+    if (j0 >= max_len) continue;
+    const uint32_t nrows = (uint32_t)(rows_per_cta < max_len - j0 ? rows_per_cta : max_len - j0);
+    const int64_t shift = side_left ? (max_len - len) : 0;  // padded row j <- source row j - shift
+    V* __restrict__ dp = reinterpret_cast<V*>(padded) + (b * max_len + j0) * vpr;
+    const V* __restrict__ vp = reinterpret_cast<const V*>(values);
+    const uint32_t n = nrows * vpr;
+    for (uint32_t v = threadIdx.x; v < n; v += blockDim.x) {
+      const uint32_t r = v / vpr;
+      const int64_t src_row = j0 + r - shift;
+      V out = fill;
+      if (src_row >= 0 && src_row < len) out = vp[(s + src_row) * vpr + (v - r * vpr)];
+      dp[v] = out;
     }
+    if (mask != nullptr)
+      for (uint32_t r = threadIdx.x; r < nrows; r += blockDim.x) {
+        const int64_t src_row = j0 + r - shift;
+        mask[b * max_len + j0 + r] = (src_row >= 0 && src_row < len) ? 1 : 0;
+      }
   }
 }
 
@@ -149,20 +141,32 @@ __global__ void inplace_scan_kernel(int32_t* __restrict__ offsets, int64_t B) {
 }
 
 template <int W>
-__global__ void from_padded_kernel(const void* __restrict__ padded,
-                                   const int32_t* __restrict__ offs, int64_t B, int64_t max_len,
-                                   int64_t row_bytes, int64_t nvec, void* __restrict__ values) {
+__global__ void __launch_bounds__(kThreads) from_padded_kernel(
+    const void* __restrict__ padded, const int32_t* __restrict__ offs, int64_t B,
+    int64_t max_len, int64_t row_bytes, int rows_per_cta, void* __restrict__ values) {
   using V = typename Vec<W>::T;
-  const int64_t vec_per_row = row_bytes / W;
-  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nvec;
-       v += (int64_t)gridDim.x * blockDim.x) {
-    int64_t row = v / vec_per_row;
-    int64_t inner = v - row * vec_per_row;
-    int64_t b = find_seq(offs, 0, B, row);
-    int64_t j = row - offs[b];
-    reinterpret_cast<V*>(values)[v] =
-        reinterpret_cast<const V*>(padded)[(b * max_len + j) * vec_per_row + inner];
+  const uint32_t vpr = (uint32_t)(row_bytes / W);
+  for (int64_t b = blockIdx.y; b < B; b += gridDim.y) {
+    const int64_t s = offs[b];
+    const int64_t len = offs[b + 1] - s;
+    const int64_t j0 = (int64_t)blockIdx.x * rows_per_cta;
+    if (j0 >= len) continue;
+    const uint32_t nrows = (uint32_t)(rows_per_cta < len - j0 ? rows_per_cta : len - j0);
+    const V* __restrict__ sp = reinterpret_cast<const V*>(padded) + (b * max_len + j0) * vpr;
+    V* __restrict__ dp = reinterpret_cast<V*>(values) + (s + j0) * vpr;
+    const uint32_t n = nrows * vpr;
+    for (uint32_t v = threadIdx.x; v < n; v += blockDim.x) dp[v] = sp[v];
   }
+}
+
+// Rows per CTA so that one CTA moves about 32 KB; grid.x covers `rows` rows,
+// grid.y the batch (capped at 65535, the kernels loop over the rest).
+dim3 gather_grid(int64_t rows, int64_t B, int64_t row_bytes, int* rows_per_cta) {
+  int64_t r = row_bytes > 0 ? (32768 + row_bytes - 1) / row_bytes : 1;
+  r = std::max<int64_t>(1, std::min<int64_t>(r, 4096));
+  *rows_per_cta = (int)r;
+  const int64_t gx = std::max<int64_t>(1, (rows + r - 1) / r);
+  return dim3((unsigned)std::min<int64_t>(gx, 2147483647), (unsigned)std::min<int64_t>(B, 65535), 1);
 }
 
 }  // namespace
@@ -171,6 +175,7 @@ __global__ void from_padded_kernel(const void* __restrict__ padded,
 using namespace scree;
 
 #define DISPATCH_WIDTH(w, KERNEL, GRID, STREAM, ...)                                      \
+  ProfScope prof_(PROF_GATHER, STREAM);                                                   \
   switch (w) {                                                                            \
     case 16: KERNEL<16><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;                \
     case 8: KERNEL<8><<<GRID, kThreads, 0, STREAM>>>(__VA_ARGS__); break;                  \
@@ -180,20 +185,22 @@ using namespace scree;
   }
 
 extern "C" int scree_pack(const void* const* src_ptrs, const void* offsets, int offs_is_i64,
-                          int64_t B, int64_t T, int64_t row_bytes, int64_t src_align, void* dst,
-                          void* stream) {
+                          int64_t B, int64_t T, int64_t max_rows, int64_t row_bytes,
+                          int64_t src_align, void* dst, void* stream) {
   SCREE_CHECK_ARG(B >= 1 && T >= 0 && row_bytes >= 0, "scree_pack: bad sizes");
   if (T == 0 || row_bytes == 0) return SCREE_OK;
   SCREE_CHECK_ARG(src_ptrs && offsets && dst, "scree_pack: null pointer");
   SCREE_CHECK_ARG(src_align >= 1, "scree_pack: src_align must be >= 1");
   // The source pointers live in device memory, so the caller states their
   // common alignment; the access width divides it, row_bytes and dst.
+  SCREE_CHECK_ARG(row_bytes < (1ll << 31), "scree_pack: rows larger than 2 GB");
   int w = pick_width(row_bytes, {(uintptr_t)dst, (uintptr_t)src_align});
-  int64_t nvec = T * row_bytes / w;
   SCREE_BIND_DEVICE(stream, dst);
   cudaStream_t s = (cudaStream_t)stream;
-  DISPATCH_WIDTH(w, pack_kernel, grid_for(nvec), s, src_ptrs, offsets, offs_is_i64, B, row_bytes,
-                 nvec, dst);
+  int rpc = 1;
+  // CTAs past a sequence's end exit at once; without a bound, T rows.
+  const dim3 grid = gather_grid(max_rows > 0 ? std::min(max_rows, T) : T, B, row_bytes, &rpc);
+  DISPATCH_WIDTH(w, pack_kernel, grid, s, src_ptrs, offsets, offs_is_i64, B, row_bytes, rpc, dst);
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
@@ -218,13 +225,20 @@ extern "C" int scree_to_padded(const void* values, const void* offsets, int offs
     SCREE_CHECK_ARG(false, "scree_to_padded: misaligned buffers for element size %lld",
                     (long long)elem_bytes);
   }
-  int64_t nvec = row_bytes == 0 ? 0 : B * max_len * (row_bytes / w);
-  int64_t work = std::max<int64_t>(nvec, B * max_len);
+  SCREE_CHECK_ARG(row_bytes < (1ll << 31), "scree_to_padded: rows larger than 2 GB");
   SCREE_BIND_DEVICE(stream, mask ? (const void*)mask : padded);
   cudaStream_t s = (cudaStream_t)stream;
-  DISPATCH_WIDTH(w, to_padded_kernel, grid_for(work), s, values, offsets, offs_is_i64, B,
-                 max_len, row_bytes == 0 ? w : row_bytes, fill16, side_left,
-                 row_bytes == 0 ? nullptr : padded, mask);
+  int rpc = 1;
+  const dim3 grid = gather_grid(max_len, B, row_bytes == 0 ? w : row_bytes, &rpc);
+  // row_bytes == 0 (empty feature dims): only the mask is written; rows of one
+  // W-byte "vector" are walked over a null padded pointer with no stores.
+  if (row_bytes == 0) {
+    to_padded_kernel<1><<<grid, kThreads, 0, s>>>(values, offsets, offs_is_i64, B, max_len, 0,
+                                                   rpc, fill16, side_left, nullptr, mask);
+  } else {
+    DISPATCH_WIDTH(w, to_padded_kernel, grid, s, values, offsets, offs_is_i64, B, max_len,
+                   row_bytes, rpc, fill16, side_left, padded, mask);
+  }
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
@@ -254,12 +268,14 @@ extern "C" int scree_from_padded(const void* padded, const int32_t* offsets, int
   SCREE_CHECK_ARG(B >= 1 && T >= 0 && max_len >= 0 && row_bytes >= 0,
                   "scree_from_padded: bad sizes");
   if (T == 0 || row_bytes == 0) return SCREE_OK;
+  SCREE_CHECK_ARG(row_bytes < (1ll << 31), "scree_from_padded: rows larger than 2 GB");
   int w = pick_width(row_bytes, {(uintptr_t)padded, (uintptr_t)values});
-  int64_t nvec = T * row_bytes / w;
   SCREE_BIND_DEVICE(stream, values);
   cudaStream_t s = (cudaStream_t)stream;
-  DISPATCH_WIDTH(w, from_padded_kernel, grid_for(nvec), s, padded, offsets, B, max_len, row_bytes,
-                 nvec, values);
+  int rpc = 1;
+  const dim3 grid = gather_grid(max_len, B, row_bytes, &rpc);
+  DISPATCH_WIDTH(w, from_padded_kernel, grid, s, padded, offsets, B, max_len, row_bytes, rpc,
+                 values);
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }

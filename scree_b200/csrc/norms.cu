@@ -67,76 +67,137 @@ __device__ __forceinline__ float ldw(const void* w, int64_t c) {
   return Cvt<WT>::to_f(reinterpret_cast<const WT*>(w)[c]);
 }
 
+template <typename T, int VW>
+__device__ __forceinline__ void unpack_vec(const Pack<T, VW>& pk, float (&out)[VW]) {
+#pragma unroll
+  for (int i = 0; i < VW; ++i) out[i] = Cvt<T>::to_f(pk.v[i]);
+}
+
+// Weight (and bias) for all C columns staged in shared memory once per CTA.
+template <typename WT>
+__device__ __forceinline__ void stage_params(float* sm, const void* w, const void* b, int C,
+                                             bool layer) {
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    sm[c] = w ? ldw<WT>(w, c) : 1.f;
+    if (layer) sm[C + c] = b ? ldw<WT>(b, c) : 0.f;
+  }
+  __syncthreads();
+}
+
 // ------------------------------------------------------------------ forward
-template <typename T, typename WT, int VW, int VPT, bool LAYER>
+// Row group of TPR threads, VPT vectors of VW elements per thread, R rows per
+// iteration (kept as packed 16-bit registers until the statistics are known).
+//   rmsnorm:   r = 1/sqrt(mean(x^2) + eps),        y = x r w
+//   layernorm: mean, biased var from (n, mean, M2), y = (x - mean) r w + b
+template <typename T, typename WT, int VW, int VPT, bool LAYER, int R>
 __global__ void __launch_bounds__(kBlock) norm_fwd_kernel(
     const T* __restrict__ x, int64_t xs, const void* __restrict__ w,
     const void* __restrict__ bias, T* __restrict__ y, int64_t ys, float* __restrict__ mean_out,
     float* __restrict__ rstd_out, int64_t rows, int C, int tpr, float eps) {
-  __shared__ float red[2 * (kBlock / 32)];
+  extern __shared__ float params[];  // [C] weight, [C] bias
+  __shared__ float red[2 * R * (kBlock / 32)];
+  stage_params<WT>(params, w, bias, C, LAYER);
   const int rpc = kBlock / tpr;
   const int g = threadIdx.x / tpr, lt = threadIdx.x % tpr;
   const int nv = C / VW;
   const float invC = 1.0f / (float)C;
-  // Uniform trip count across the CTA (group_sum has __syncthreads).
-  const int64_t iters = (rows + (int64_t)gridDim.x * rpc - 1) / ((int64_t)gridDim.x * rpc);
+  const int64_t step = (int64_t)gridDim.x * rpc;
+  const int64_t iters = (rows + R * step - 1) / (R * step);  // uniform across the CTA
   for (int64_t it = 0; it < iters; ++it) {
-    const int64_t row = (it * gridDim.x + blockIdx.x) * rpc + g;
-    const bool live = row < rows;
-    float xv[VPT][VW];
-    float s[1] = {0.f};
+    int64_t row[R];
+    bool live[R];
+    Pack<T, VW> xr[R][VPT];
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int vi = lt + i * tpr;
-      if (live && vi < nv) {
-        load_vec<T, VW>(x + row * xs + (int64_t)vi * VW, xv[i]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < VW; ++e) xv[i][e] = 0.f;
-      }
-#pragma unroll
-      for (int e = 0; e < VW; ++e) s[0] += LAYER ? xv[i][e] : xv[i][e] * xv[i][e];
+    for (int k = 0; k < R; ++k) {
+      row[k] = (R * it + k) * step + (int64_t)blockIdx.x * rpc + g;
+      live[k] = row[k] < rows;
     }
-    group_sum<1>(s, tpr, red);
-    float mu = 0.f, r;
-    if (LAYER) {
-      mu = s[0] * invC;
-      float q[1] = {0.f};
+#pragma unroll
+    for (int k = 0; k < R; ++k)
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int vi = lt + i * tpr;
-        if (vi < nv)
+        if (live[k] && vi < nv)
+          xr[k][i] = *reinterpret_cast<const Pack<T, VW>*>(x + row[k] * xs + (int64_t)vi * VW);
+        else
 #pragma unroll
-          for (int e = 0; e < VW; ++e) {
-            float d = xv[i][e] - mu;
-            q[0] += d * d;
-          }
+          for (int e = 0; e < VW; ++e) xr[k][i].v[e] = Cvt<T>::from_f(0.f);
       }
-      group_sum<1>(q, tpr, red + (kBlock / 32));
-      r = 1.0f / sqrtf(q[0] * invC + eps);
+    float mu[R], r[R];
+    if (LAYER) {
+      // Shifted-data variance: with K = the row's first element,
+      //   mean = K + S1/C,  var = (S2 - S1^2/C)/C,  S1 = sum(x-K), S2 = sum((x-K)^2),
+      // one combined reduction; the shift keeps S2 - S1^2/C free of cancellation
+      // for rows whose mean is large against their spread.
+      float sv[2 * R], K[R];
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        K[k] = live[k] ? Cvt<T>::to_f(x[row[k] * xs]) : 0.f;
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i)
+          if (lt + i * tpr < nv) {
+            float xv[VW];
+            unpack_vec<T, VW>(xr[k][i], xv);
+#pragma unroll
+            for (int e = 0; e < VW; ++e) {
+              const float d = xv[e] - K[k];
+              s1 += d;
+              s2 = fmaf(d, d, s2);
+            }
+          }
+        sv[2 * k] = s1;
+        sv[2 * k + 1] = s2;
+      }
+      group_sum<2 * R>(sv, tpr, red);
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        const float d1 = sv[2 * k] * invC;
+        mu[k] = K[k] + d1;
+        const float var = fmaxf(sv[2 * k + 1] * invC - d1 * d1, 0.f);
+        r[k] = 1.0f / sqrtf(var + eps);
+      }
     } else {
-      r = 1.0f / sqrtf(s[0] * invC + eps);
+      float ss[R];
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        ss[k] = 0.f;
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) {
+          float xv[VW];
+          unpack_vec<T, VW>(xr[k][i], xv);
+#pragma unroll
+          for (int e = 0; e < VW; ++e) ss[k] = fmaf(xv[e], xv[e], ss[k]);
+        }
+      }
+      group_sum<R>(ss, tpr, red);
+#pragma unroll
+      for (int k = 0; k < R; ++k) {
+        mu[k] = 0.f;
+        r[k] = 1.0f / sqrtf(ss[k] * invC + eps);
+      }
     }
-    if (live) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (!live[k]) continue;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int vi = lt + i * tpr;
         if (vi < nv) {
-          float out[VW];
+          float xv[VW], out[VW];
+          unpack_vec<T, VW>(xr[k][i], xv);
+          const float* wp = params + vi * VW;
 #pragma unroll
           for (int e = 0; e < VW; ++e) {
-            const int64_t c = (int64_t)vi * VW + e;
-            float t = (xv[i][e] - mu) * r;
-            if (w) t *= ldw<WT>(w, c);
-            if (LAYER && bias) t += ldw<WT>(bias, c);
-            out[e] = t;
+            const float t = (xv[e] - mu[k]) * r[k] * wp[e];
+            out[e] = LAYER ? t + wp[C + e] : t;
           }
-          store_vec<T, VW>(y + row * ys + (int64_t)vi * VW, out);
+          store_vec<T, VW>(y + row[k] * ys + (int64_t)vi * VW, out);
         }
       }
       if (lt == 0) {
-        if (rstd_out) rstd_out[row] = r;
-        if (LAYER && mean_out) mean_out[row] = mu;
+        if (rstd_out) rstd_out[row[k]] = r[k];
+        if (LAYER && mean_out) mean_out[row[k]] = mu[k];
       }
     }
   }
@@ -147,12 +208,16 @@ __global__ void __launch_bounds__(kBlock) norm_fwd_kernel(
 //   rmsnorm:   dx = r * (g - xhat * mean(g * xhat))
 //   layernorm: dx = r * (g - mean(g) - xhat * mean(g * xhat))
 //   dweight = sum_rows dy * xhat,  dbias = sum_rows dy
+// x and dy stay packed in registers; the weight comes from shared memory; the
+// per-thread dweight / dbias partials are written to `part_*` at the end.
 template <typename T, typename WT, int VW, int VPT, bool LAYER>
 __global__ void __launch_bounds__(kBlock) norm_bwd_kernel(
     const T* __restrict__ dy, const T* __restrict__ x, const void* __restrict__ w,
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in, T* __restrict__ dx,
     float* __restrict__ part_w, float* __restrict__ part_b, int64_t rows, int C, int tpr) {
+  extern __shared__ float params[];  // [C] weight
   __shared__ float red[2 * (kBlock / 32)];
+  stage_params<WT>(params, w, nullptr, C, false);
   const int rpc = kBlock / tpr;
   const int g = threadIdx.x / tpr, lt = threadIdx.x % tpr;
   const int nv = C / VW;
@@ -168,28 +233,36 @@ __global__ void __launch_bounds__(kBlock) norm_bwd_kernel(
     const bool live = row < rows;
     const float r = live ? rstd_in[row] : 0.f;
     const float mu = (LAYER && live) ? mean_in[row] : 0.f;
-    float xh[VPT][VW], gv[VPT][VW];
-    float s[2] = {0.f, 0.f};  // sum(g), sum(g * xhat)
+    Pack<T, VW> xr[VPT], dr[VPT];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
       const int vi = lt + i * tpr;
       if (live && vi < nv) {
-        float xx[VW], dd[VW];
-        load_vec<T, VW>(x + row * (int64_t)C + (int64_t)vi * VW, xx);
-        load_vec<T, VW>(dy + row * (int64_t)C + (int64_t)vi * VW, dd);
-#pragma unroll
-        for (int e = 0; e < VW; ++e) {
-          const int64_t c = (int64_t)vi * VW + e;
-          xh[i][e] = (xx[e] - mu) * r;
-          gv[i][e] = w ? dd[e] * ldw<WT>(w, c) : dd[e];
-          accw[i][e] += dd[e] * xh[i][e];
-          if (LAYER) accb[i][e] += dd[e];
-          s[0] += gv[i][e];
-          s[1] += gv[i][e] * xh[i][e];
-        }
+        xr[i] = *reinterpret_cast<const Pack<T, VW>*>(x + row * (int64_t)C + (int64_t)vi * VW);
+        dr[i] = *reinterpret_cast<const Pack<T, VW>*>(dy + row * (int64_t)C + (int64_t)vi * VW);
       } else {
 #pragma unroll
-        for (int e = 0; e < VW; ++e) xh[i][e] = gv[i][e] = 0.f;
+        for (int e = 0; e < VW; ++e) xr[i].v[e] = dr[i].v[e] = Cvt<T>::from_f(0.f);
+      }
+    }
+    float s[2] = {0.f, 0.f};  // sum(g), sum(g * xhat)
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = lt + i * tpr;
+      if (vi < nv) {
+        float xx[VW], dd[VW];
+        unpack_vec<T, VW>(xr[i], xx);
+        unpack_vec<T, VW>(dr[i], dd);
+        const float* wp = params + vi * VW;
+#pragma unroll
+        for (int e = 0; e < VW; ++e) {
+          const float xh = (xx[e] - mu) * r;
+          const float gv = dd[e] * wp[e];
+          accw[i][e] = fmaf(dd[e], xh, accw[i][e]);
+          if (LAYER) accb[i][e] += dd[e];
+          s[0] += gv;
+          s[1] = fmaf(gv, xh, s[1]);
+        }
       }
     }
     group_sum<2>(s, tpr, red);
@@ -200,9 +273,15 @@ __global__ void __launch_bounds__(kBlock) norm_bwd_kernel(
       for (int i = 0; i < VPT; ++i) {
         const int vi = lt + i * tpr;
         if (vi < nv) {
-          float out[VW];
+          float xx[VW], dd[VW], out[VW];
+          unpack_vec<T, VW>(xr[i], xx);
+          unpack_vec<T, VW>(dr[i], dd);
+          const float* wp = params + vi * VW;
 #pragma unroll
-          for (int e = 0; e < VW; ++e) out[e] = r * (gv[i][e] - mg - xh[i][e] * mgx);
+          for (int e = 0; e < VW; ++e) {
+            const float xh = (xx[e] - mu) * r;
+            out[e] = r * (dd[e] * wp[e] - mg - xh * mgx);
+          }
           store_vec<T, VW>(dx + row * (int64_t)C + (int64_t)vi * VW, out);
         }
       }
@@ -249,14 +328,21 @@ struct Plan {
   int tpr;  // threads per row
   int vpt;  // vectors per thread
   int grid;
+  int rows_per_iter;  // forward: rows a row group loads before reducing (1 or 2)
+  int smem;           // dynamic shared memory: staged weight (and bias)
   bool ok;
 };
 
-Plan plan_for(int64_t rows, int64_t C, int esize, bool aligned16, int max_vpt, bool bwd) {
+Plan plan_for(int64_t rows, int64_t C, int esize, bool aligned16, int max_vpt, bool bwd,
+              bool layer = false) {
   Plan p{};
   p.vw = (aligned16 && (C * esize) % 16 == 0) ? 16 / esize : 1;
   const int64_t nv = C / p.vw;
+  // Prefer few vectors per thread (registers for x and, in the backward, dy and
+  // the partial sums); wider rows use more threads.
+  const int target_vpt = bwd ? (layer ? 2 : 4) : 4;  // layernorm bwd carries dbias too
   int tpr = 32;
+  while (tpr < kBlock && (nv + tpr - 1) / tpr > target_vpt) tpr <<= 1;
   while (tpr < 1024 && (nv + tpr - 1) / tpr > max_vpt) tpr <<= 1;
   int64_t vpt = (nv + tpr - 1) / tpr;
   int v = 1;
@@ -266,20 +352,48 @@ Plan plan_for(int64_t rows, int64_t C, int esize, bool aligned16, int max_vpt, b
   if (tpr > kBlock) p.ok = false;
   p.tpr = tpr;
   p.vpt = v;
+  if (!p.ok) {  // rows too wide for one CTA: rejected by the caller
+    p.grid = 1;
+    return p;
+  }
   const int rpc = kBlock / tpr;
   const int64_t need = (rows + rpc - 1) / rpc;
-  const int64_t cap = (int64_t)num_sms() * (bwd ? 2 : 8);
+  // Grids measured best at cfg3 (hidden 4096): 4 CTAs per SM forward, 2 backward
+  // (fewer dweight partial rows); launches also cap at the real occupancy.
+  const int64_t cap = (int64_t)num_sms() * (bwd ? 2 : 4);
+  p.rows_per_iter = 1;
+  // Staged parameters: weight (+ bias in the layernorm forward, sized for both).
+  p.smem = (int)(C * sizeof(float) * (bwd ? 1 : 2));
+  if (p.smem > 200 * 1024) p.ok = false;
   p.grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, cap));
   return p;
 }
 
+// Launch with the plan's dynamic shared memory (opting in above 48 KB).
+template <typename K, typename... Args>
+void launch_smem(K kernel, Plan& p, cudaStream_t s, Args... args) {
+  if (p.smem > 48 * 1024)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
+  // No more CTAs than fit at once (a second partial wave would idle most SMs):
+  // the kernels grid-stride over rows, so any grid is correct.
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kBlock, p.smem) == cudaSuccess &&
+      occ > 0)
+    p.grid = std::max(1, std::min(p.grid, occ * num_sms()));
+  kernel<<<p.grid, kBlock, p.smem, s>>>(args...);
+}
+
 template <typename T, typename WT, int VW, bool LAYER>
-int launch_fwd_vpt(const Plan& p, cudaStream_t s, const void* x, int64_t xs, const void* w,
+int launch_fwd_vpt(Plan& p, cudaStream_t s, const void* x, int64_t xs, const void* w,
                    const void* b, void* y, int64_t ys, float* mean, float* rstd, int64_t rows,
                    int C, float eps) {
 #define SCREE_FWD(V)                                                                        \
-  norm_fwd_kernel<T, WT, VW, V, LAYER><<<p.grid, kBlock, 0, s>>>(                           \
-      (const T*)x, xs, w, b, (T*)y, ys, mean, rstd, rows, C, p.tpr, eps)
+  if (p.rows_per_iter == 1)                                                                 \
+    launch_smem(norm_fwd_kernel<T, WT, VW, V, LAYER, 1>, p, s,                              \
+        (const T*)x, xs, w, b, (T*)y, ys, mean, rstd, rows, C, p.tpr, eps);                 \
+  else                                                                                      \
+    launch_smem(norm_fwd_kernel<T, WT, VW, V, LAYER, 2>, p, s,                              \
+        (const T*)x, xs, w, b, (T*)y, ys, mean, rstd, rows, C, p.tpr, eps)
   ProfScope prof(PROF_NORM_FWD, s);
   switch (p.vpt) {
     case 1: SCREE_FWD(1); break;
@@ -294,7 +408,7 @@ int launch_fwd_vpt(const Plan& p, cudaStream_t s, const void* x, int64_t xs, con
 }
 
 template <typename T, typename WT, bool LAYER>
-int launch_fwd(const Plan& p, cudaStream_t s, const void* x, int64_t xs, const void* w,
+int launch_fwd(Plan& p, cudaStream_t s, const void* x, int64_t xs, const void* w,
                const void* b, void* y, int64_t ys, float* mean, float* rstd, int64_t rows, int C,
                float eps) {
   if (p.vw == 1) return launch_fwd_vpt<T, WT, 1, LAYER>(p, s, x, xs, w, b, y, ys, mean, rstd, rows, C, eps);
@@ -302,11 +416,11 @@ int launch_fwd(const Plan& p, cudaStream_t s, const void* x, int64_t xs, const v
 }
 
 template <typename T, typename WT, int VW, bool LAYER>
-int launch_bwd_vpt(const Plan& p, cudaStream_t s, const void* dy, const void* x, const void* w,
+int launch_bwd_vpt(Plan& p, cudaStream_t s, const void* dy, const void* x, const void* w,
                    const float* mean, const float* rstd, void* dx, float* pw, float* pb,
                    int64_t rows, int C) {
 #define SCREE_BWD(V)                                                                       \
-  norm_bwd_kernel<T, WT, VW, V, LAYER><<<p.grid, kBlock, 0, s>>>(                          \
+  launch_smem(norm_bwd_kernel<T, WT, VW, V, LAYER>, p, s,                                   \
       (const T*)dy, (const T*)x, w, mean, rstd, (T*)dx, pw, pb, rows, C, p.tpr)
   ProfScope prof(PROF_NORM_BWD, s);
   switch (p.vpt) {
@@ -320,7 +434,7 @@ int launch_bwd_vpt(const Plan& p, cudaStream_t s, const void* dy, const void* x,
 }
 
 template <typename T, typename WT, bool LAYER>
-int launch_bwd(const Plan& p, cudaStream_t s, const void* dy, const void* x, const void* w,
+int launch_bwd(Plan& p, cudaStream_t s, const void* dy, const void* x, const void* w,
                const float* mean, const float* rstd, void* dx, float* pw, float* pb,
                int64_t rows, int C) {
   if (p.vw == 1) return launch_bwd_vpt<T, WT, 1, LAYER>(p, s, dy, x, w, mean, rstd, dx, pw, pb, rows, C);
@@ -376,9 +490,15 @@ int norm_fwd(const void* x, int64_t xs, const void* w, const void* b, int w_dtyp
 }
 
 int64_t bwd_partials(int64_t rows, int64_t C) {
-  // Upper bound over dtypes: grid <= 2 * SMs, rows per CTA <= kBlock / 32.
-  (void)rows;
-  return (int64_t)num_sms() * 2 * (kBlock / 32);
+  // Partial rows = grid x rows per CTA of the backward plan; the maximum over
+  // the 16-bit and 32-bit layouts (and over aligned / unaligned access).
+  int64_t best = 1;
+  for (int es : {2, 4})
+    for (bool a16 : {true, false}) {
+      Plan p = plan_for(rows, C, es, a16, 4, true, false);  // layernorm plans use fewer rows/CTA
+      if (p.ok) best = std::max<int64_t>(best, (int64_t)p.grid * (kBlock / p.tpr));
+    }
+  return best;
 }
 
 template <bool LAYER>
@@ -400,11 +520,13 @@ int norm_bwd(const void* dy, const void* x, const void* w, int w_dtype, const fl
   }
   const bool a16 = ((uintptr_t)x % 16 == 0) && ((uintptr_t)dy % 16 == 0) &&
                    ((uintptr_t)dx % 16 == 0);
-  Plan p = plan_for(rows, C, es, a16, 4, true);
+  Plan p = plan_for(rows, C, es, a16, 4, true, LAYER);
   if (!p.ok) {
     set_last_error("norm bwd: feature dim %lld too large", (long long)C);
     return SCREE_ERR_UNSUPPORTED;
   }
+  // Partial rows: one per row group of the planned grid (the launch may use
+  // fewer CTAs, then fewer rows are written and reduced).
   const int64_t P = (int64_t)p.grid * (kBlock / p.tpr);
   float* pw = nullptr;
   float* pb = nullptr;
@@ -424,11 +546,11 @@ int norm_bwd(const void* dy, const void* x, const void* w, int w_dtype, const fl
   if (rc != SCREE_OK) return rc;
   const unsigned cgrid = (unsigned)((C + 31) / 32);
   if (want_w) {
-    column_sum_kernel<<<cgrid, 256, 0, s>>>(pw, P, (int)C, dw);
+    column_sum_kernel<<<cgrid, 256, 0, s>>>(pw, (int64_t)p.grid * (kBlock / p.tpr), (int)C, dw);
     SCREE_LAUNCH_CHECK();
   }
   if (want_b) {
-    column_sum_kernel<<<cgrid, 256, 0, s>>>(pb, P, (int)C, db);
+    column_sum_kernel<<<cgrid, 256, 0, s>>>(pb, (int64_t)p.grid * (kBlock / p.tpr), (int)C, db);
     SCREE_LAUNCH_CHECK();
   }
   return SCREE_OK;

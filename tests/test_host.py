@@ -45,7 +45,7 @@ def test_argument_validation_without_gpu():
         _lib.check(rc, "attn")
     rc = lib.scree_attn_bwd(None, None, None, None, None, None, None, 0, 1, 10, 1, 64, 2, 0, 1.0, 0, None, None, None, None, 0, None)
     assert rc == _lib.SCREE_ERR_INVALID  # fp32 attention is rejected
-    assert lib.scree_pack(None, None, 0, 0, 0, 0, 16, None, None) == _lib.SCREE_ERR_INVALID
+    assert lib.scree_pack(None, None, 0, 0, 0, 0, 0, 16, None, None) == _lib.SCREE_ERR_INVALID
     assert lib.scree_to_padded(None, None, 0, 1, 1, 4, 3, None, 0, None, None, None) == _lib.SCREE_ERR_INVALID
 
 
@@ -132,3 +132,13 @@ def test_triton_module_path_is_drop_in():
     for name in ("varlen_attention_triton", "varlen_attention_triton_autograd", "varlen_layernorm_triton", "varlen_rmsnorm_triton", "TRITON_AVAILABLE"):
         assert hasattr(t, name)
     assert t.TRITON_AVAILABLE is True
+
+
+def test_norm_workspace_size_on_odd_and_wide_rows():
+    """The backward workspace query plans every layout, including rows too wide
+    for one CTA (rejected later by the kernel), without faulting."""
+    from scree_b200 import _lib
+
+    lib = _lib.load()
+    for rows, C in [(100, 33), (19794, 4096), (1, 8), (64, 8192), (10, 100000), (0, 7)]:
+        assert lib.scree_norm_bwd_workspace_size(rows, C) >= 8 * C
