@@ -393,12 +393,12 @@ def main():
     from scree_b200.kernels.native import varlen_attention_triton_autograd
 
     # Shard plan: LPT on L^2 (attention cost), broadcast from rank 0.
-    plan = workloads.lpt_partition([L * L for L in lengths], world)
+    from scree_b200 import shard
+
+    plan = shard.plan_shards(lengths, world, cost="attention")
     if world > 1:
-        obj = [plan]
-        dist.broadcast_object_list(obj, src=0)
-        assert obj[0] == plan, "shard plan differs across ranks"
-    mine = [lengths[i] for i in plan[rank]]
+        plan = shard.broadcast_plan(plan)
+    mine = [lengths[i] for i in sorted(plan[rank])]
     T = sum(mine)
     dt = getattr(torch, args.dtype_name)
     g = torch.Generator(device=dev).manual_seed(1234 + 17 * rank)

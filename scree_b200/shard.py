@@ -1,0 +1,119 @@
+"""Whole-sequence sharding of a packed batch across ranks (one process per GPU).
+
+Sequences are independent in every op of the varlen path (attention has no
+cross-sequence term, norms are per token), so a batch splits across GPUs with
+no reduction: each rank runs the kernels on its own sub-batch.  This module
+holds the host side of that:
+
+  * plan_shards   longest-processing-time-first assignment of sequences to
+                  ranks by cost (L^2 for attention, L for norms / gathers);
+  * broadcast_plan  rank 0's plan sent to every rank (torch.distributed, any
+                  backend), with a check that every rank derived the same one;
+  * LocalShard    a rank's sub-batch: its sequence indices, local offsets and
+                  the global token rows they come from;
+  * gather_to_rank0  per-rank outputs collected on rank 0 in global order
+                  (pad-to-max all_gather, since ranks hold different row counts).
+Multi-GPU runs use NCCL over NVLink for these collectives; the CPU tests use gloo.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Sequence
+
+import numpy as np
+
+from .workloads import lpt_partition
+
+
+def plan_shards(lengths: Sequence[int], world: int, cost: str = "attention") -> List[List[int]]:
+    """Sequence indices per rank, balanced by L^2 ("attention") or L ("tokens")."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    if cost == "attention":
+        costs = [float(L) * float(L) for L in lengths]
+    elif cost == "tokens":
+        costs = [float(L) for L in lengths]
+    else:
+        raise ValueError(f"unknown cost model {cost!r}")
+    return lpt_partition(costs, world)
+
+
+def imbalance(lengths: Sequence[int], plan: List[List[int]], cost: str = "attention") -> float:
+    """max rank cost / mean rank cost of a plan (1.0 = perfect)."""
+    f = (lambda L: float(L) ** 2) if cost == "attention" else float
+    loads = [sum(f(lengths[i]) for i in part) for part in plan]
+    mean = sum(loads) / len(loads)
+    return max(loads) / mean if mean > 0 else 1.0
+
+
+def broadcast_plan(plan: List[List[int]], group=None) -> List[List[int]]:
+    """Send rank 0's plan to every rank; raise if any rank had computed another."""
+    import torch.distributed as dist
+
+    obj = [plan]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    if obj[0] != plan:
+        raise RuntimeError("shard plan differs across ranks (inputs or seeds disagree)")
+    return obj[0]
+
+
+@dataclass(frozen=True)
+class LocalShard:
+    """One rank's part of a packed batch."""
+
+    seqs: tuple          # global sequence indices, ascending
+    lengths: tuple       # their lengths
+    offsets: np.ndarray  # local (B_r + 1,) int64 offsets
+    rows: np.ndarray     # global token row of each local row, (T_r,) int64
+
+    @property
+    def tokens(self) -> int:
+        return int(self.offsets[-1])
+
+
+def local_shard(global_offsets: Sequence[int], plan: List[List[int]], rank: int) -> LocalShard:
+    go = np.asarray(global_offsets, dtype=np.int64)
+    seqs = tuple(sorted(plan[rank]))
+    lengths = tuple(int(go[i + 1] - go[i]) for i in seqs)
+    offs = np.zeros(len(seqs) + 1, dtype=np.int64)
+    offs[1:] = np.cumsum(lengths)
+    rows = (
+        np.concatenate([np.arange(go[i], go[i + 1], dtype=np.int64) for i in seqs])
+        if seqs
+        else np.zeros(0, dtype=np.int64)
+    )
+    return LocalShard(seqs, lengths, offs, rows)
+
+
+def gather_to_rank0(local_values, shard: LocalShard, total_rows: int, group=None):
+    """All ranks pass their (T_r, ...) values; rank 0 receives the (T, ...) tensor
+    in global row order, other ranks receive None.  Pads to the largest T_r and
+    uses all_gather (NCCL on GPUs, gloo on CPU)."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    dev = local_values.device
+    n = torch.tensor([local_values.shape[0]], dtype=torch.int64, device=dev)
+    ns = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(ns, n, group=group)
+    counts = [int(c.item()) for c in ns]
+    tmax = max(counts) if counts else 0
+    feat = tuple(local_values.shape[1:])
+    padded = torch.zeros((tmax, *feat), dtype=local_values.dtype, device=dev)
+    padded[: local_values.shape[0]] = local_values
+    rows = torch.full((tmax,), -1, dtype=torch.int64, device=dev)
+    rows[: shard.rows.shape[0]] = torch.as_tensor(shard.rows, device=dev)
+    bufs = [torch.empty_like(padded) for _ in range(world)]
+    rbufs = [torch.empty_like(rows) for _ in range(world)]
+    dist.all_gather(bufs, padded, group=group)
+    dist.all_gather(rbufs, rows, group=group)
+    if rank != 0:
+        return None
+    out = torch.empty((total_rows, *feat), dtype=local_values.dtype, device=dev)
+    for c, b, r in zip(counts, bufs, rbufs):
+        if c:
+            out[r[:c]] = b[:c]
+    return out

@@ -1,0 +1,114 @@
+"""Multi-rank host logic of the whole-sequence sharding, on CPU with gloo
+(world size 2): plan broadcast and agreement, coverage of every token, the
+gather back to global order, and detection of a failed rank by timeout."""
+
+import datetime
+import multiprocessing as mp
+import os
+import socket
+import traceback
+
+import numpy as np
+import pytest
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, mode, q):
+    try:
+        import torch
+        import torch.distributed as dist
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=5 if mode == "fail" else 60))
+        from scree_b200 import shard, workloads
+
+        lengths = workloads.cfg4_lengths()
+        offs = np.concatenate([[0], np.cumsum(lengths)])
+        plan = shard.plan_shards(lengths, world)
+        if mode == "disagree" and rank == 1:
+            plan = [plan[1], plan[0]]
+        if mode == "fail" and rank == 1:
+            raise SystemExit(0)  # this rank leaves before the first collective
+        try:
+            plan = shard.broadcast_plan(plan)
+        except RuntimeError as e:
+            # A peer that disagrees, or one that is gone (gloo raises on the
+            # closed connection or after the process-group timeout).
+            q.put((rank, "plan-mismatch" if "differs" in str(e) else "error", str(e)[:200]))
+            return
+        mine = shard.local_shard(offs, plan, rank)
+        # Every rank "computes" on its rows: here, the global row index itself.
+        vals = torch.as_tensor(mine.rows, dtype=torch.float64).reshape(-1, 1) * 2.0
+        if mode == "fail":
+            try:
+                shard.gather_to_rank0(vals, mine, int(offs[-1]))
+                q.put((rank, "no-error", ""))
+            except Exception as e:  # the missing rank must surface as an error
+                q.put((rank, "error", type(e).__name__))
+            return
+        out = shard.gather_to_rank0(vals, mine, int(offs[-1]))
+        if rank == 0:
+            ok = torch.equal(out[:, 0], torch.arange(int(offs[-1]), dtype=torch.float64) * 2.0)
+            q.put((rank, "gathered", ok))
+        else:
+            q.put((rank, "sent", out is None))
+        dist.destroy_process_group()
+    except BaseException:
+        q.put((rank, "exception", traceback.format_exc()))
+
+
+def _run(mode, world=2, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    out = []
+    while not q.empty():
+        out.append(q.get())
+    return sorted(out, key=lambda t: t[0])
+
+
+def test_plan_covers_and_balances():
+    from scree_b200 import shard, workloads
+
+    lengths = workloads.cfg4_lengths()
+    offs = np.concatenate([[0], np.cumsum(lengths)])
+    for world in (1, 2, 4, 8):
+        plan = shard.plan_shards(lengths, world)
+        assert sorted(i for p in plan for i in p) == list(range(len(lengths)))
+        assert shard.imbalance(lengths, plan) < 1.02
+        rows = np.concatenate([shard.local_shard(offs, plan, r).rows for r in range(world)])
+        assert np.array_equal(np.sort(rows), np.arange(offs[-1]))
+
+
+def test_two_ranks_gather_global_order():
+    res = _run("ok")
+    assert [r[1] for r in res] == ["gathered", "sent"], res
+    assert res[0][2] is True and res[1][2] is True
+
+
+def test_two_ranks_detect_plan_disagreement():
+    res = _run("disagree")
+    assert any(r[1] == "plan-mismatch" for r in res), res
+
+
+def test_missing_rank_is_an_error_not_a_hang():
+    res = _run("fail", timeout=90)
+    assert res and res[0][0] == 0 and res[0][1] in ("error", "exception"), res
