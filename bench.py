@@ -513,13 +513,13 @@ def main():
         if world > 1:
             dist.all_reduce(e_ms, op=dist.ReduceOp.MAX)
         e_step = float(e_ms[0]) / args.e2e_steps
-        nbytes = q.numel() * q.element_size()
+        nbytes = int(total_T) * H * D * q.element_size()  # one (T, H, D) tensor, all ranks
         e2e = {
             "value": total_T / (e_step / 1e3),
             "unit": "tokens/s",
             "ms_per_step": e_step,
-            "h2d_bytes_per_step": int(4 * nbytes * world),
-            "d2h_bytes_per_step": int(4 * nbytes * world),
+            "h2d_bytes_per_step": int(4 * nbytes),  # q, k, v, dO
+            "d2h_bytes_per_step": int(4 * nbytes),  # out, dq, dk, dv
             "path": "varlen_attention_triton_autograd with pinned host q/k/v/dO in, out/dq/dk/dv back to pinned host",
         }
         del dq_
@@ -545,7 +545,7 @@ def main():
             "data": "synthetic",
             "config": workload_config(args, lengths, H, D, causal, world),
             "tflops": tflops,
-            "tflops_frac_of_peak": tflops / peak_tf,
+            "tflops_frac_of_peak": tflops / (peak_tf * world),
             "roofline": {
                 "kernel": "attn_bwd_kernel<128, bf16, causal> (dK/dV/dQ, 10*H*D*pairs FLOPs)",
                 "bound": "tensor",
