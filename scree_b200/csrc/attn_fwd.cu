@@ -56,8 +56,10 @@ struct FwdCfg {
   static constexpr int CHUNK = SWB / 2;           // elements per swizzle row
   static constexpr int NCHUNK = D / CHUNK;
   static constexpr uint32_t SWZ = SWB == 128 ? SW_128B : SW_64B;
-  static constexpr int KSTAGES = 3;
-  static constexpr int VSTAGES = D == 128 ? 2 : 3;
+  // K_j frees after both S GEMMs of iteration j-1, V_j only after both PV GEMMs
+  // of iteration j; V gets the deeper ring (it has one iteration less slack).
+  static constexpr int KSTAGES = D == 128 ? 2 : 3;
+  static constexpr int VSTAGES = 3;
   static constexpr int Q_BYTES = BM * D * 2;   // one query tile
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int OFF_Q = 0;              // Q_A, Q_B
@@ -245,21 +247,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     regs_dec<kRegsOther>();
     if (elect_one()) {
       const int nX[2] = {nA, nB};
+      // Descriptors differ per k-step only in the start address (bits [0,14) =
+      // addr >> 4), so they are built once per buffer and advanced by adding
+      // the step's byte offset >> 4 (addresses stay below 256 KB: no carry).
+      auto kstep_off = [](int kk, int rows) -> uint32_t {
+        const int e = kk * 16;
+        return (uint32_t)(((e / C::CHUNK) * rows * C::SWB + (e % C::CHUNK) * 2) >> 4);
+      };
       auto issue_s = [&](int x, int j) {
         const uint32_t kb = sK + (j % C::KSTAGES) * C::KV_BYTES;
         const uint32_t qb = sQ + x * C::Q_BYTES;
+        const uint64_t dq = kmajor_desc<D>(qb, BM, 0), dk = kmajor_desc<D>(kb, BN, 0);
+        const uint32_t dt = tmem + C::COL_S + x * BN;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16_ss(tmem + C::COL_S + x * BN, kmajor_desc<D>(qb, BM, kk),
-                      kmajor_desc<D>(kb, BN, kk), IDESC_S, kk > 0 ? 1u : 0u);
+          umma_f16_ss(dt, dq + kstep_off(kk, BM), dk + kstep_off(kk, BN), IDESC_S,
+                      kk > 0 ? 1u : 0u);
         umma_commit(&s_full[x]);
       };
       auto issue_pv = [&](int x, int j) {
         const uint32_t vb = sV + (j % C::VSTAGES) * C::KV_BYTES;
         const uint32_t pt = tmem + C::COL_S + x * BN;
+        const uint64_t dv = v_desc<D>(vb, 0);
+        const uint32_t dt = tmem + C::COL_O + x * D;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns per step
-          umma_f16_ts(tmem + C::COL_O + x * D, pt + kk * 8, v_desc<D>(vb, kk), IDESC_O,
+          umma_f16_ts(dt, pt + kk * 8, dv + (uint32_t)((kk * 16 * C::SWB) >> 4), IDESC_O,
                       (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&pv_done[x]);
       };
@@ -287,8 +300,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (j < nX[x]) {
             if (!(ok = mbar_wait(&p_full[x], j & 1, abort_flag, p.status, 2 + 4 * x))) break;
             tc_fence_after();
+#ifdef SCREE_TRACE
+            const long long t_is0 = clock64();
+#endif
             issue_pv(x, j);
             if (j + 1 < nX[x]) issue_s(x, j + 1);
+#ifdef SCREE_TRACE
+            SCREE_TRACE_ADD(21, clock64() - t_is0);
+#endif
           }
         }
         if (!ok) break;
@@ -316,6 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int j = 0; j < nmine; ++j) {
       ok = mbar_wait(&s_full[x], j & 1, abort_flag, p.status, 7);
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+#ifdef SCREE_TRACE
+      const long long t_sm0 = clock64();
+#endif
       tc_fence_after();
       // One TMEM load of the whole 128-column row (a single wait::ld).
       float s[BN];
@@ -331,13 +353,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BN; ++c)
           if (k0 + c > lim) s[c] = -INFINITY;
       }
+      // Row max: 8 independent chains of three-input max (two values per step).
       float mx8[8];
 #pragma unroll
       for (int a = 0; a < 8; ++a) mx8[a] = s[a];
 #pragma unroll
-      for (int c = 8; c < BN; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int c = 8; c < BN; c += 16)
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mx8[a] = fmax3(mx8[a], s[c + a], s[c + 8 + a < BN ? c + 8 + a : c + a]);
+      const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                             fmaxf(mx8[6], mx8[7]));
       const float m_cand = mx * sl2;
       float alpha = 1.f;
       bool need = false;
@@ -352,17 +377,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
       // Exponentiate and pack: each pair of S values dies as its packed word appears.
-      float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // Exponentiate and pack, two columns per packed f32x2 FMA / add; each pair of
+      // S values dies as its packed 16-bit word appears.
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_eff, -m_eff);
+      uint64_t rs4[4] = {0ull, 0ull, 0ull, 0ull};  // (+0.0f, +0.0f) pairs
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN; c += 2) {
-        const float e0 = ex2_approx(fmaf(s[c], sl2, -m_eff));
-        const float e1 = ex2_approx(fmaf(s[c + 1], sl2, -m_eff));
-        rs8[c & 7] += e0;
-        rs8[(c + 1) & 7] += e1;
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, negm2), x0, x1);
+        const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
+        const uint64_t e01 = f2_pack(e0, e1);
+        rs4[(c / 2) & 3] = f2_add(rs4[(c / 2) & 3], e01);
         pk[c / 2] = Pk2<T>::pack(e0, e1);
       }
-      const float rs = ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      float ra, rb;
+      f2_unpack(f2_add(f2_add(rs4[0], rs4[1]), f2_add(rs4[2], rs4[3])), ra, rb);
+      const float rs = ra + rb;
       if (j >= 1) {
         // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
         // before P_X(j) overwrites the columns it read.  It already is in the
@@ -388,6 +419,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[x]);
+#ifdef SCREE_TRACE
+      SCREE_TRACE_ADD(20, clock64() - t_sm0);
+#endif
     }
     // ------------------------------------------------------------ epilogue
     if (ok && nmine > 0) {
