@@ -27,7 +27,8 @@
 // [62] = CTA lifetime cycles, [63] = query tiles processed.
 static __device__ unsigned long long g_bwd_trace[64];
 #define SCREE_TRACE_ADD(site, cyc) \
-  do { if ((threadIdx.x & 31) == 0) atomicAdd(&g_bwd_trace[(site) & 63], (unsigned long long)(cyc)); } while (0)
+  do { if ((threadIdx.x & 31) == 0 || (site) == 12) atomicAdd(&scree_trace_sm[(site) & 63], (unsigned long long)(cyc)); } while (0)
+static __shared__ unsigned long long scree_trace_sm[64];  // per-CTA, flushed at exit
 #endif
 #include "attn_common.cuh"
 
@@ -35,12 +36,13 @@ namespace scree {
 namespace {
 
 constexpr int BN = 128;  // keys per CTA
-// Warpgroup 0: P^T / dS^T (softmax) warps; warpgroup 1: dQ reduction warps;
-// warpgroup 2: TMA warp, MMA warp, two idle warps.  Launched at 168 registers
-// per thread (65,536 / 384); warpgroup 0 grows to 240, warpgroup 2 shrinks to 80:
-// 128 x 240 + 128 x 168 + 128 x 80 = 62,464 <= 384 x 168 = 64,512.
-constexpr int kThreads = 384;
-constexpr int kRegsSoftmax = 240, kRegsOther = 80;
+// Warpgroups 0-1: P^T / dS^T warps (warps w and w+4 share TMEM lanes 32(w%4)..,
+// each takes half of a tile's query columns); warpgroup 2: TMA warp, MMA warp,
+// two idle warps; warpgroup 3: dQ reduction warps.  Launched at 128 registers per
+// thread (65,536 / 512); the P/dS warpgroups grow to 152, warpgroup 2 shrinks to
+// 80 and warpgroup 3 to 120: 256 x 152 + 128 x 80 + 128 x 120 = 64,512 <= 65,536.
+constexpr int kThreads = 512;
+constexpr int kRegsSoftmax = 152, kRegsOther = 80, kRegsDq = 120;
 
 template <int D>
 struct BwdCfg {
@@ -136,25 +138,27 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-// Named barriers over the 128 threads of warps 0-3 and of warps 4-7.
+// Named barriers over the 256 P/dS threads (warps 0-7) and the 128 dQ threads.
 __device__ __forceinline__ void softmax_group_sync() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync 1, 256;" ::: "memory");
 }
 __device__ __forceinline__ void dq_group_sync() {
   asm volatile("bar.sync 2, 128;" ::: "memory");
 }
 
-// Row-major [BN][BQ] 16-bit tile in 128B swizzle: write the BQ values of row kr.
-template <typename T, int BQ>
-__device__ __forceinline__ void write_row_sw128(uint8_t* base, int kr, const float* v) {
+// Row-major [BN][BQ] 16-bit tile in 128B swizzle: write N values of row kr
+// starting at column 8 * u0.
+template <typename T, int N>
+__device__ __forceinline__ void write_row_sw128(uint8_t* base, int kr, const float* v, int u0) {
   const int sw = kr & 7;
 #pragma unroll
-  for (int u = 0; u < BQ / 8; ++u) {
+  for (int i = 0; i < N / 8; ++i) {
+    const int u = u0 + i;
     uint4 w;
-    w.x = Pk2b<T>::pack(v[u * 8 + 0], v[u * 8 + 1]);
-    w.y = Pk2b<T>::pack(v[u * 8 + 2], v[u * 8 + 3]);
-    w.z = Pk2b<T>::pack(v[u * 8 + 4], v[u * 8 + 5]);
-    w.w = Pk2b<T>::pack(v[u * 8 + 6], v[u * 8 + 7]);
+    w.x = Pk2b<T>::pack(v[i * 8 + 0], v[i * 8 + 1]);
+    w.y = Pk2b<T>::pack(v[i * 8 + 2], v[i * 8 + 3]);
+    w.z = Pk2b<T>::pack(v[i * 8 + 4], v[i * 8 + 5]);
+    w.w = Pk2b<T>::pack(v[i * 8 + 6], v[i * 8 + 7]);
     const int blk = u >> 3, uu = u & 7;
     *reinterpret_cast<uint4*>(base + blk * BN * 128 + kr * 128 + ((uu ^ sw) << 4)) = w;
   }
@@ -224,6 +228,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long t_cta0 = clock64();
 #endif
 
+#ifdef SCREE_TRACE
+  if (threadIdx.x < 64) scree_trace_sm[threadIdx.x] = 0;
+#endif
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
     for (int s = 0; s < C::STAGES; ++s) {
@@ -232,8 +239,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(dp_full, 1);
-    mbar_init(p_full, 128);
-    mbar_init(ds_full, 128);
+    mbar_init(p_full, 256);
+    mbar_init(ds_full, 256);
     mbar_init(p_free, 1);
     mbar_init(ds_free, 1);
     mbar_init(dq_full, 1);
@@ -356,60 +363,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       umma_commit(acc_done);
     }
-  } else if (warp >= 10) {
+  } else if (warp == 10 || warp == 11) {
     regs_dec<kRegsOther>();  // idle: only completes warpgroup 2's register release
-  } else if (warp < 4) {
+  } else if (warp < 8) {
     // ------------------------------------------------------------ P^T / dS^T
     regs_inc<kRegsSoftmax>();
-    const int kr = threadIdx.x;  // key row within the tile == TMEM lane
+    constexpr int QH = BQ / 2;                // query columns per warp half
+    const int hf = warp >> 2;                 // which half of the tile's queries
+    const int kr = (warp & 3) * 32 + (threadIdx.x & 31);  // key row == TMEM lane
     const int kidx = k0 + kr;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const bool key_ok = kidx < L;
     const float sl2 = p.scale_log2;
     const float* lse_h = p.lse2T + (int64_t)h * p.T + row0;
     const float* del_h = p.deltaT + (int64_t)h * p.T + row0;
+    const int t256 = threadIdx.x;             // 0..255 over both warpgroups
     bool ok = true;
-    // LSE / Delta of query tile `it` (queries past L read as 0; masked below).
-    // Thread kr fetches entry kr of the 2*BQ values; they are loaded one tile
-    // ahead so the global latency overlaps the current tile's work.
-    auto fetch = [&](int it_, float& a, float& b) {
-      const int q0_ = (i_first + it_) * BQ;
-      if (BQ == 64) {
-        const int q = q0_ + (kr & 63);
-        a = q < L ? (kr < 64 ? lse_h[q] : del_h[q]) : 0.f;
-      } else {
-        const int q = q0_ + kr;
-        a = q < L ? lse_h[q] : 0.f;
-        b = q < L ? del_h[q] : 0.f;
-      }
+    // LSE / Delta of query tile `it` staged as [BQ lse][BQ delta] (queries past L
+    // read as 0; masked below), fetched one tile ahead.
+    auto fetch = [&](int it_) -> float {
+      if (t256 >= 2 * BQ) return 0.f;
+      const int q = (i_first + it_) * BQ + (t256 % BQ);
+      return q < L ? (t256 < BQ ? lse_h[q] : del_h[q]) : 0.f;
     };
-    float pre_a = 0.f, pre_b = 0.f;
-    fetch(0, pre_a, pre_b);
+    float pre = fetch(0);
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (i_first + it) * BQ;
-      float* lse_s = lds + (it & 1) * 2 * BQ;
-      float* del_s = lse_s + BQ;
-      if (BQ == 64) {
-        lds[(it & 1) * 2 * BQ + kr] = pre_a;  // [0,64) lse, [64,128) delta
-      } else {
-        lse_s[kr] = pre_a;
-        del_s[kr] = pre_b;
-      }
-      if (it + 1 < n_it) fetch(it + 1, pre_a, pre_b);
+      const int qh0 = q0 + hf * QH;           // first query of this half
+      float* lse_s = lds + (it & 1) * 2 * BQ + hf * QH;
+      float* del_s = lds + (it & 1) * 2 * BQ + BQ + hf * QH;
+      if (t256 < 2 * BQ) lds[(it & 1) * 2 * BQ + t256] = pre;
+      if (it + 1 < n_it) pre = fetch(it + 1);
       softmax_group_sync();
       const bool need_mask = (q0 + BQ > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
-      // ---- P^T row from S^T
+      // ---- P^T (this half's QH queries) from S^T
       ok = mbar_wait(s_full, it & 1, abort_flag, p.status, 28);
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
-      float pr[BQ];
+      float pr[QH];
 #pragma unroll
-      for (int c = 0; c < BQ / 32; ++c)
-        tmem_ld32(lane_base + C::COL_S + c * 32, *reinterpret_cast<float(*)[32]>(&pr[c * 32]));
+      for (int c = 0; c < QH / 32; ++c)
+        tmem_ld32(lane_base + C::COL_S + hf * QH + c * 32,
+                  *reinterpret_cast<float(*)[32]>(&pr[c * 32]));
       tmem_wait_ld();
-      uint32_t pk[BQ / 2];
+      uint32_t pk[QH / 2];
 #pragma unroll
-      for (int c4 = 0; c4 < BQ / 4; ++c4) {
+      for (int c4 = 0; c4 < QH / 4; ++c4) {
         const float4 l4 = reinterpret_cast<const float4*>(lse_s)[c4];  // one LDS.128
         const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
@@ -417,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int c = c4 * 4 + e;
           float xv = ex2_approx(fmaf(pr[c], sl2, -lv[e]));
           if (need_mask) {
-            const int q = q0 + c;
+            const int q = qh0 + c;
             const bool valid = key_ok && q < L && (!CAUSAL || q >= kidx);
             xv = valid ? xv : 0.f;
           }
@@ -430,10 +429,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(p_free, (it - 1) & 1, abort_flag, p.status, 29);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       }
-      // P^T (16-bit, two per column) over the first BQ/2 columns of S^T.
-#pragma unroll
-      for (int c = 0; c < BQ / 64; ++c)
-        tmem_st32u(lane_base + C::COL_S + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[c * 32]));
+      // P^T (16-bit, two per column): this half's QH/2 columns of S^T's first BQ/2.
+      tmem_st_packed<QH / 2>(lane_base + C::COL_S + hf * (QH / 2), pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -442,9 +439,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < BQ / 32; ++c) {
+      for (int c = 0; c < QH / 32; ++c) {
         float dp[32];
-        tmem_ld32(lane_base + C::COL_DP + c * 32, dp);
+        tmem_ld32(lane_base + C::COL_DP + hf * QH + c * 32, dp);
         tmem_wait_ld();
 #pragma unroll
         for (int e4 = 0; e4 < 8; ++e4) {
@@ -456,23 +453,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
 #pragma unroll
-      for (int c = 0; c < BQ / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
+      for (int c = 0; c < QH / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
       if (it > 0) {
         ok = mbar_wait(ds_free, (it - 1) & 1, abort_flag, p.status, 31);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       }
       // dS^T: into TMEM over dP^T's first columns (A operand of dK) and into
       // smem (B operand of the dQ GEMM).
-#pragma unroll
-      for (int c = 0; c < BQ / 64; ++c)
-        tmem_st32u(lane_base + C::COL_DP + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[c * 32]));
-      write_row_sw128<T, BQ>(smem + C::OFF_DS, kr, pr);
+      tmem_st_packed<QH / 2>(lane_base + C::COL_DP + hf * (QH / 2), pk);
+      write_row_sw128<T, QH>(smem + C::OFF_DS, kr, pr, hf * (QH / 8));
       tmem_wait_st();
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(ds_full);
     }
-    // ---- dK, dV epilogue
+    // ---- dK, dV epilogue: 32-column chunk c belongs to half c % 2
     if (ok) {
       ok = mbar_wait(acc_done, 0, abort_flag, p.status, 32);
       ok = __all_sync(0xffffffff, ok);
@@ -488,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         T* dst = pass == 0 ? dvrow : dkrow;
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
+          if ((c & 1) != hf) continue;
           float v[32];
           tmem_ld32(lane_base + col + c * 32, v);
           tmem_wait_ld();
@@ -506,9 +502,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ------------------------------------------------------------ dQ reduction warps 4-7
-    const int ln = threadIdx.x - 128;  // TMEM lane: feature d (DQT) or query row
-    const uint32_t lane_base = tmem + ((uint32_t)((warp - 4) * 32) << 16);
+    // ------------------------------------------------------------ dQ reduction warps 12-15
+    regs_dec<kRegsDq>();
+    const int ln = threadIdx.x - 384;  // TMEM lane: feature d (DQT) or query row
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
     const float sc = p.scale;
     for (int it = 0; it < n_it; ++it) {
       const int q0 = (i_first + it) * BQ;
@@ -564,9 +561,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 #ifdef SCREE_TRACE
   if (threadIdx.x == 0) {
-    atomicAdd(&g_bwd_trace[62], (unsigned long long)(clock64() - t_cta0));
-    atomicAdd(&g_bwd_trace[63], (unsigned long long)n_it);
+    scree_trace_sm[62] += (unsigned long long)(clock64() - t_cta0);
+    scree_trace_sm[63] += (unsigned long long)(n_it);
   }
+  __syncthreads();
+  if (threadIdx.x < 64) atomicAdd(&g_bwd_trace[threadIdx.x], scree_trace_sm[threadIdx.x]);
 #endif
   if (warp == 9) {
     tc_fence_after();

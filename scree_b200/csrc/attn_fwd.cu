@@ -33,7 +33,8 @@
 // [30] = CTA lifetime cycles, [31] = key tiles processed.
 static __device__ unsigned long long g_fwd_trace[32];
 #define SCREE_TRACE_ADD(site, cyc) \
-  do { if ((threadIdx.x & 31) == 0 || (site) == 12) atomicAdd(&g_fwd_trace[(site) & 31], (unsigned long long)(cyc)); } while (0)
+  do { if ((threadIdx.x & 31) == 0 || (site) == 12) atomicAdd(&scree_trace_sm[(site) & 31], (unsigned long long)(cyc)); } while (0)
+static __shared__ unsigned long long scree_trace_sm[32];  // per-CTA, flushed at exit
 #endif
 #include "attn_common.cuh"
 
@@ -179,6 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const long long t_cta0 = clock64();
 #endif
 
+#ifdef SCREE_TRACE
+  if (threadIdx.x < 32) scree_trace_sm[threadIdx.x] = 0;
+#endif
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < C::KSTAGES; ++s) {
@@ -460,9 +464,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 #ifdef SCREE_TRACE
   if (threadIdx.x == 0) {
-    atomicAdd(&g_fwd_trace[30], (unsigned long long)(clock64() - t_cta0));
-    atomicAdd(&g_fwd_trace[31], (unsigned long long)n_kv);
+    scree_trace_sm[30] += (unsigned long long)(clock64() - t_cta0);
+    scree_trace_sm[31] += (unsigned long long)(n_kv);
   }
+  __syncthreads();
+  if (threadIdx.x < 32) atomicAdd(&g_fwd_trace[threadIdx.x], scree_trace_sm[threadIdx.x]);
 #endif
   if (warp == 9) {
     tc_fence_after();

@@ -232,6 +232,27 @@ __device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t (&v)[3
       "r"(v[29]), "r"(v[30]), "r"(v[31])
       : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns from registers (raw bits).
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
+      : "memory");
+}
+// N (16 or a multiple of 32) packed columns from registers.
+template <int N>
+__device__ __forceinline__ void tmem_st_packed(uint32_t taddr, const uint32_t* v) {
+  if constexpr (N == 16) {
+    tmem_st16u(taddr, v);
+  } else {
+#pragma unroll
+    for (int c = 0; c < N / 32; ++c)
+      tmem_st32u(taddr + c * 32, *reinterpret_cast<const uint32_t(*)[32]>(v + c * 32));
+  }
+}
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile(

@@ -155,11 +155,21 @@ def test_attention_cfg4_full_size_sampled(cuda):
             sub = [t[s:e, h : h + 1] for t in (q, k, v, do)]
             ref = attn_reference(*sub, [e - s], True)
             got = [t[s:e, h : h + 1] for t in (out, lse, dq, dk, dv)]
+            emul = None
             for name, gt, rf in zip(("out", "lse", "dq", "dk", "dv"), got, ref):
                 if name == "lse":
                     err = excess(to64(gt), rf, 1e-3, 0.0)
                 else:
                     err = excess(to64(gt), rf, 1e-2, 2.0**-8)
+                if err > 0 and name in ("dq", "dk", "dv"):
+                    # Same second criterion as _check: within twice the error of
+                    # the fp64 oracle with the kernel's 16-bit rounding points.
+                    if emul is None:
+                        emul = dict(zip(("dq", "dk", "dv"), attn_bwd_emulated(*sub, [e - s], True, torch.bfloat16)))
+                    e_got, e_emul = max_err(to64(gt), rf), max_err(emul[name], rf)
+                    assert e_got <= 2 * e_emul, (
+                        f"seq {b} (L={e-s}) head {h} {name}: max err {e_got:.3e} > 2 x emulation {e_emul:.3e}")
+                    continue
                 assert err <= 0, f"seq {b} (L={e-s}) head {h} {name}: out of bounds by {err}"
 
 
