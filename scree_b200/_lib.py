@@ -10,7 +10,10 @@ import ctypes
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libscree_b200.so"
+import os
+
+# SCREE_B200_LIB points at another build of the library (benchmark A/B runs).
+LIB_PATH = Path(os.environ.get("SCREE_B200_LIB", Path(__file__).resolve().parent / "libscree_b200.so"))
 
 SCREE_OK = 0
 SCREE_ERR_INVALID = 1
