@@ -280,6 +280,8 @@ def run_norm_suite(args):
     _, rstd = native._rmsnorm_fwd(x, w, 1e-5, True)
     _, mean, rstd_l = native._layernorm_fwd(x, w, bias, 1e-5, True)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    sm_y = native.varlen_softmax_packed(x, offs)
+    sm_dx = torch.empty_like(x)
     B = len(lengths)
     ops = {
         "rmsnorm_fwd": (lambda: native.varlen_rmsnorm_triton(x, w, 1e-5), 2 * T * C * b + 4 * C),
@@ -289,6 +291,8 @@ def run_norm_suite(args):
         "pack": (lambda: scree.pack(rows), 2 * T * C * b + 4 * (B + 1)),
         "to_padded": (lambda: scree.to_padded(arr), T * C * b + B * Lmax * C * b + B * Lmax),
         "from_padded": (lambda: scree.from_padded(padded, mask), B * Lmax + 2 * T * C * b),
+        "softmax_fwd": (lambda: native.varlen_softmax_packed(x, offs), 2 * T * C * b),
+        "softmax_bwd": (lambda: native._softmax_call(_lib.load().scree_softmax_bwd, "sm bwd", offs, sm_dx, dy, sm_y), 3 * T * C * b),
     }
     peaks, kind = load_peaks()
     hbm = float(peaks["hbm_gbs"])
@@ -298,6 +302,7 @@ def run_norm_suite(args):
             fn()
         # Kernel-only time from the library's CUDA-event hooks around each
         # launch; the 256 MB flush is written before every launch.
+        # (the softmax kernels report under the norm fwd / bwd event kinds)
         kind_ = _lib.PROF_NORM_FWD if name.endswith("_fwd") else (_lib.PROF_NORM_BWD if name.endswith("_bwd") else _lib.PROF_GATHER)
         times = []
         _lib.profile_read(kind_)
@@ -326,7 +331,7 @@ def run_norm_suite(args):
         cpu = {"value": 2 * T * C * b / t_cpu / 1e9, "unit": "GB/s", "cores": len(os.sched_getaffinity(0)),
                "kind": "port", "sample": f"rmsnorm_fwd on the full cfg3 batch (fp32 numpy oracle), {t_cpu:.3f} s"}
     line = {
-        "metric": "varlen norms / gathers HBM GB/s (cfg3)",
+        "metric": "varlen norms / softmax / gathers HBM GB/s (cfg3)",
         "value": res["rmsnorm_fwd"]["gb_s"],
         "unit": "GB/s",
         "n_gpus": 1,

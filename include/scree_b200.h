@@ -142,6 +142,18 @@ int scree_layernorm_bwd(const void* dy, const void* x, const void* weight, int w
                         float* dbias, int64_t rows, int64_t C, int dtype, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------ softmax
+ * Varlen softmax along the ragged dimension: within each sequence, independently
+ * for every feature column of the (T, F) row-major values.
+ * Replaces: scree/kernels/reference/varlen_softmax.py:13-63 varlen_softmax (the
+ * reference ships no GPU kernel for it).  fp32 statistics; y same dtype as x. */
+int scree_softmax_fwd(const void* x, const void* offsets, int offs_is_i64, int64_t B, int64_t T,
+                      int64_t F, int dtype, void* y, void* stream);
+/* Its backward: dx = y * (dy - sum over the sequence's rows of dy * y), per column
+ * (torch autograd of reference/varlen_softmax.py:41-48 computes the same). */
+int scree_softmax_bwd(const void* dy, const void* y, const void* offsets, int offs_is_i64,
+                      int64_t B, int64_t T, int64_t F, int dtype, void* dx, void* stream);
+
 /* ------------------------------------------------------------------ gathers
  * pack: concatenate B contiguous row-major sources along rows.
  * Replaces: scree/_core.py:97-141 pack (torch branch :108-113, torch.cat).

@@ -21,6 +21,8 @@ from .varlen import (  # noqa: F401
     pack,
     rmsnorm_bwd,
     rmsnorm_fwd,
+    softmax_bwd,
+    softmax_fwd,
     to_padded,
     unpack,
 )

@@ -191,3 +191,31 @@ def layernorm_bwd(dy, x, weight=None, bias=None, eps=1e-5, dtype=np.float64):
     dw = (dy * xh).reshape(-1, C).sum(axis=0) if weight is not None else None
     db = dy.reshape(-1, C).sum(axis=0) if bias is not None else None
     return dx, dw, db
+
+
+# --------------------------------------------------------------------------- softmax
+def softmax_fwd(values, offsets, dtype=np.float64):
+    """Per-sequence softmax along axis 0 (src/scree/kernels/reference/varlen_softmax.py:55-61)."""
+    x = np.asarray(values, dtype=dtype)
+    out = np.empty_like(x)
+    for i in range(len(offsets) - 1):
+        s0, e0 = int(offsets[i]), int(offsets[i + 1])
+        if e0 == s0:
+            continue
+        row = x[s0:e0]
+        ex = np.exp(row - row.max(axis=0, keepdims=True))
+        out[s0:e0] = ex / ex.sum(axis=0, keepdims=True)
+    return out
+
+
+def softmax_bwd(dy, y, offsets, dtype=np.float64):
+    """Gradient of softmax_fwd: dx = y * (dy - sum_rows(dy * y)) per sequence."""
+    dy = np.asarray(dy, dtype=dtype)
+    y = np.asarray(y, dtype=dtype)
+    dx = np.empty_like(y)
+    for i in range(len(offsets) - 1):
+        s0, e0 = int(offsets[i]), int(offsets[i + 1])
+        if e0 == s0:
+            continue
+        dx[s0:e0] = y[s0:e0] * (dy[s0:e0] - (dy[s0:e0] * y[s0:e0]).sum(axis=0, keepdims=True))
+    return dx

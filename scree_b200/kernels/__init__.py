@@ -5,6 +5,7 @@ Same call shapes as scree/kernels/reference/__init__.py:7-17 for the hot path:
   varlen_rmsnorm(arr, weight=None, eps=1e-6) -> Array reference/varlen_rmsnorm.py:18
   varlen_layernorm(arr, weight=None, bias=None, eps=1e-5) -> Array
                                                       reference/varlen_layernorm.py:14
+  varlen_softmax(arr) -> Array                        reference/varlen_softmax.py:13
 Every call runs the sm_100a kernels of libscree_b200 and is differentiable
 (torch autograd), like the reference's torch branch.  Output Arrays reuse the
 input's offsets object (reference/varlen_attention.py:140).
@@ -15,7 +16,7 @@ from __future__ import annotations
 from .._core import Array, _is_torch
 from . import native
 
-__all__ = ["varlen_attention", "varlen_rmsnorm", "varlen_layernorm", "native"]
+__all__ = ["varlen_attention", "varlen_rmsnorm", "varlen_layernorm", "varlen_softmax", "native"]
 
 
 def _check_cuda(arr: Array, name: str) -> None:
@@ -48,3 +49,12 @@ def varlen_layernorm(arr: Array, weight=None, bias=None, eps: float = 1e-5) -> A
     _check_cuda(arr, "varlen_layernorm")
     y = native.varlen_layernorm_autograd(arr.values, weight, bias, eps)
     return Array(values=y, offsets=arr.offsets, ragged_dim=arr.ragged_dim, _host=arr._host)
+
+
+def varlen_softmax(arr: Array) -> Array:
+    """Softmax along the ragged dimension, per sequence and feature column."""
+    _check_cuda(arr, "varlen_softmax")
+    if arr.ragged_dim != 0:
+        raise NotImplementedError("varlen_softmax supports ragged_dim=0 only in v0.1")
+    y = native.varlen_softmax_packed(arr.values, arr.offsets)
+    return Array(values=y, offsets=arr.offsets, ragged_dim=0, _host=arr._host)

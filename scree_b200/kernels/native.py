@@ -33,6 +33,7 @@ __all__ = [
     "varlen_layernorm_backward",
     "varlen_rmsnorm_autograd",
     "varlen_layernorm_autograd",
+    "varlen_softmax_packed",
 ]
 
 
@@ -340,3 +341,45 @@ def varlen_rmsnorm_autograd(x, weight=None, eps: float = 1e-6):
 def varlen_layernorm_autograd(x, weight=None, bias=None, eps: float = 1e-5):
     """Differentiable varlen LayerNorm (forward and backward on sm_100a kernels)."""
     return _LayerNorm.apply(x, weight, bias, eps)
+
+
+# --------------------------------------------------------------------------- softmax
+
+
+def _softmax_call(fn, what, offs, out, *tensors):
+    cu, is64 = _offsets_arg(offs, tensors[0].device)
+    T = tensors[0].shape[0]
+    F = 1
+    for d in tensors[0].shape[1:]:
+        F *= int(d)
+    with torch.cuda.device(tensors[0].device):
+        rc = fn(*[t.data_ptr() for t in tensors], cu.data_ptr(), is64, cu.numel() - 1, T, F,
+                _lib.dtype_code(tensors[0].dtype), out.data_ptr(), _lib.stream_ptr(tensors[0].device))
+    _lib.check(rc, what)
+
+
+class _VarlenSoftmax(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, values, offsets):
+        x = values.contiguous()
+        y = torch.empty_like(x)
+        _softmax_call(_lib.load().scree_softmax_fwd, "varlen_softmax", offsets, y, x)
+        ctx.save_for_backward(y, offsets)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        y, offsets = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = torch.empty_like(y)
+        _softmax_call(_lib.load().scree_softmax_bwd, "varlen_softmax backward", offsets, dx, dy, y)
+        return dx, None
+
+
+def varlen_softmax_packed(values, offsets):
+    """Softmax along the ragged (first) dim of packed (T, ...) values within each
+    sequence [offsets[b], offsets[b+1]), per feature column; differentiable.
+    Tensor-level form of scree/kernels/reference/varlen_softmax.py:13."""
+    assert values.is_cuda, "varlen_softmax requires CUDA tensors"
+    assert values.dtype in (torch.float16, torch.bfloat16, torch.float32), "fp16, bf16 or fp32 only"
+    return _VarlenSoftmax.apply(values, offsets)

@@ -115,6 +115,21 @@ def norm_case(scree, ref, torch, lengths, C, with_weight, with_bias, seed, eps_r
     return res
 
 
+def softmax_case(scree, ref, torch, lengths, feat, seed):
+    rng = np.random.default_rng(seed)
+    T = sum(lengths)
+    x = (3.0 * rng.standard_normal((T, *feat))).astype(np.float32)
+    dy = rng.standard_normal((T, *feat)).astype(np.float32)
+    offs = np.zeros(len(lengths) + 1, dtype=np.int32)
+    offs[1:] = np.cumsum(lengths)
+    y = ref.varlen_softmax(scree.Array(values=x.astype(np.float64), offsets=offs)).values
+    tx = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    ty = ref.varlen_softmax(scree.Array(values=tx, offsets=torch.tensor(offs))).values
+    ty.backward(torch.tensor(dy, dtype=torch.float64))
+    return {"lengths": np.array(lengths), "x": x, "dy": dy, "y": y.astype(np.float32),
+            "y_torch": ty.detach().numpy().astype(np.float32), "dx": tx.grad.numpy().astype(np.float32)}
+
+
 def gather_case(scree, lengths, feat, seed, fill):
     rng = np.random.default_rng(seed)
     seqs = [rng.integers(-1000, 1000, size=(n, *feat)).astype(np.int32) for n in lengths]
@@ -154,6 +169,11 @@ def main():
         "norm_c128": norm_case(scree, ref, torch, [3, 5, 2, 60], 128, True, True, 3, 1e-6, 1e-5),
     }
     for name, c in norms.items():
+        np.savez_compressed(OUT / f"golden_{name}.npz", **c)
+    for name, c in {
+        "softmax_ref_small": softmax_case(scree, ref, torch, [3, 5, 2], (4,), 6),
+        "softmax_2d": softmax_case(scree, ref, torch, [1, 7, 40, 13], (3, 24), 7),
+    }.items():
         np.savez_compressed(OUT / f"golden_{name}.npz", **c)
     gathers = {
         "gather_2d": gather_case(scree, [3, 1, 5, 2], (3,), 4, -7),

@@ -100,3 +100,23 @@ def test_oracle_roundtrip_left_padding_mask():
     vals, offs = oracle.pack([np.ones((2, 3)), np.ones((4, 3))])
     p, m = oracle.to_padded(vals, offs, side="left")
     assert m.tolist() == [[False, False, True, True], [True, True, True, True]]
+
+
+@pytest.mark.parametrize("name", ["softmax_ref_small", "softmax_2d"])
+def test_oracle_softmax_matches_reference(name):
+    """varlen_softmax (reference/varlen_softmax.py): values and torch-autograd gradient."""
+    g = load_golden(name)
+    offs = np.concatenate([[0], np.cumsum(g["lengths"])])
+    y = oracle.softmax_fwd(g["x"], offs)
+    np.testing.assert_allclose(y, g["y"], atol=1e-6)
+    np.testing.assert_allclose(y, g["y_torch"], atol=1e-6)
+    np.testing.assert_allclose(oracle.softmax_bwd(g["dy"], y, offs), g["dx"], atol=1e-5)
+
+
+def test_oracle_softmax_columns_sum_to_one():
+    """reference tests/test_varlen_kernels.py:119-140: per-sequence sums are 1."""
+    rng = np.random.default_rng(0)
+    vals, offs = oracle.pack([rng.standard_normal((n, 3)) for n in [3, 5, 2]])
+    y = oracle.softmax_fwd(vals, offs)
+    for rows in oracle.unpack(y, offs):
+        np.testing.assert_allclose(rows.sum(axis=0), np.ones(3), atol=1e-12)
