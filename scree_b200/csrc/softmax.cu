@@ -52,20 +52,36 @@ __global__ void __launch_bounds__(kThreads) softmax_fwd_kernel(const T* __restri
     m[i] = -INFINITY;
     s[i] = 0.f;
   }
-  if (col_ok)
-    for (int64_t r = r0 + warp; r < r1; r += kWarps) {
+  if (col_ok) {
+    // Rows in groups of 4 per warp: one max update and one rescale per group
+    // (no divergent per-element branch), loads of the group issued together.
+    constexpr int G = 4;
+    int64_t r = r0 + warp;
+    for (; r + (G - 1) * kWarps < r1; r += G * kWarps) {
+      float v[G][VW];
+#pragma unroll
+      for (int g = 0; g < G; ++g) sload<T, VW>(x + (r + g * kWarps) * F + c0, v[g]);
+#pragma unroll
+      for (int i = 0; i < VW; ++i) {
+        const float mn = fmaxf(fmaxf(m[i], fmaxf(v[0][i], v[1][i])), fmaxf(v[2][i], v[3][i]));
+        float acc = (m[i] == -INFINITY) ? 0.f : s[i] * __expf(m[i] - mn);
+#pragma unroll
+        for (int g = 0; g < G; ++g) acc += __expf(v[g][i] - mn);
+        s[i] = acc;
+        m[i] = mn;
+      }
+    }
+    for (; r < r1; r += kWarps) {  // remaining rows one at a time
       float v[VW];
       sload<T, VW>(x + r * F + c0, v);
 #pragma unroll
       for (int i = 0; i < VW; ++i) {
-        if (v[i] > m[i]) {  // rescale the running sum to the new max
-          s[i] = s[i] * __expf(m[i] - v[i]) + 1.f;
-          m[i] = v[i];
-        } else {
-          s[i] += __expf(v[i] - m[i]);
-        }
+        const float mn = fmaxf(m[i], v[i]);
+        s[i] = ((m[i] == -INFINITY) ? 0.f : s[i] * __expf(m[i] - mn)) + __expf(v[i] - mn);
+        m[i] = mn;
       }
     }
+  }
 #pragma unroll
   for (int i = 0; i < VW; ++i) {
     sm_m[warp][lane * VW + i] = m[i];
