@@ -4,6 +4,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <type_traits>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -97,9 +98,30 @@ template <> struct Cvt<__half> {
   static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
 };
 template <> struct Cvt<__nv_bfloat16> {
-  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  // bf16 is the top half of an fp32: widening is a 16-bit shift (integer ALU,
+  // exact), which keeps conversion-heavy loops off the special-function pipe.
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) {
+    return __uint_as_float(static_cast<uint32_t>(__bfloat16_as_ushort(x)) << 16);
+  }
   static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
 };
+
+// N floats -> N values of T; 16-bit types convert two per instruction.
+template <typename T, int N>
+__device__ __forceinline__ void cvt_from_f(const float* v, T* o) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && N % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i)
+      reinterpret_cast<__nv_bfloat162*>(o)[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  } else if constexpr (std::is_same<T, __half>::value && N % 2 == 0) {
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i)
+      reinterpret_cast<__half2*>(o)[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; ++i) o[i] = Cvt<T>::from_f(v[i]);
+  }
+}
 
 // Offsets may be int32 or int64; read either as int64.
 __device__ __forceinline__ int64_t load_offset(const void* offs, int is_i64, int64_t i) {

@@ -15,6 +15,7 @@
 // second kernel in a fixed order (deterministic, no atomics).
 #include <algorithm>
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace scree {
 namespace {
@@ -32,8 +33,7 @@ __device__ __forceinline__ void load_vec(const T* p, float (&out)[VW]) {
 template <typename T, int VW>
 __device__ __forceinline__ void store_vec(T* p, const float (&in)[VW]) {
   Pack<T, VW> pk;
-#pragma unroll
-  for (int i = 0; i < VW; ++i) pk.v[i] = Cvt<T>::from_f(in[i]);
+  cvt_from_f<T, VW>(in, pk.v);
   *reinterpret_cast<Pack<T, VW>*>(p) = pk;
 }
 
@@ -203,6 +203,171 @@ __global__ void __launch_bounds__(kBlock) norm_fwd_kernel(
   }
 }
 
+// Parameters for the streamed kernels, staged as VW/4 planes of float4: plane k
+// holds elements 4k..4k+3 of every VW-element vector, so lanes reading
+// consecutive vectors read consecutive 16 bytes (no bank conflicts).  The bias
+// (layernorm forward) follows at offset C.
+template <typename WT, int VW>
+__device__ __forceinline__ void stage_params_planar(float* sm, const void* w, const void* b, int C,
+                                                    bool layer) {
+  const int nv = C / VW;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const int v = c / VW, e = c % VW;
+    const int idx = ((e >> 2) * nv + v) * 4 + (e & 3);
+    sm[idx] = w ? ldw<WT>(w, c) : 1.f;
+    if (layer) sm[C + idx] = b ? ldw<WT>(b, c) : 0.f;
+  }
+  __syncthreads();
+}
+template <int VW>
+__device__ __forceinline__ void load_params(const float* planes, int nv, int v, float (&out)[VW]) {
+#pragma unroll
+  for (int k = 0; k < VW / 4; ++k) {
+    const float4 f = reinterpret_cast<const float4*>(planes)[k * nv + v];
+    out[4 * k] = f.x;
+    out[4 * k + 1] = f.y;
+    out[4 * k + 2] = f.z;
+    out[4 * k + 3] = f.w;
+  }
+}
+
+// ------------------------------------------------------- forward, streamed
+// Rows of at least 1 KB (C = 4096 in 16-bit is 8 KB): every warp owns whole rows
+// (rows warp_id, warp_id + all_warps, ...) and a private ring of `stages` row
+// slots in shared memory, filled by 1-D bulk copies (cp.async.bulk) that lane 0
+// issues `stages` rows ahead.  Statistics are warp shuffles only, so warps never
+// wait on each other and each SM keeps (stages - 1) rows per warp in flight
+// while it computes.  Pass 1 reads the slot for the statistics, pass 2 reads it
+// again for y, which is stored straight from registers (16-byte vectors).
+constexpr int kStreamSite = 92;
+
+__device__ __forceinline__ bool bar_wait_drain(uint64_t* bar, uint32_t parity) {
+  // Exit path only: wait (at most the same limit) for a copy still in flight so
+  // the CTA never retires with a bulk copy targeting its shared memory.
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_timer_ns() - t0 > SCREE_WAIT_LIMIT_NS) return false;
+  return true;
+}
+
+template <typename T, typename WT, bool LAYER>
+__global__ void __launch_bounds__(kBlock) norm_fwd_stream_kernel(
+    const T* __restrict__ x, int64_t xs, const void* __restrict__ w,
+    const void* __restrict__ bias, T* __restrict__ y, int64_t ys, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int64_t rows, int C, int stages, float eps, int* status) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ int abort_flag;
+  constexpr int VW = 16 / sizeof(T);
+  const int nwarps = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t row_bytes = (uint32_t)C * sizeof(T);
+  const int nv = C / VW;
+  float* params = reinterpret_cast<float*>(smem_raw);
+  const size_t poff = ((size_t)C * sizeof(float) * (LAYER ? 2 : 1) + 127) & ~(size_t)127;
+  unsigned char* ring = smem_raw + poff + (size_t)warp * stages * row_bytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + poff + (size_t)nwarps * stages * row_bytes) +
+                   warp * stages;
+  if (threadIdx.x == 0) abort_flag = 0;
+  if (lane == 0)
+    for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
+  fence_mbar_init();
+  stage_params_planar<WT, VW>(params, w, bias, C, LAYER);  // ends with __syncthreads
+
+  const int64_t NW = (int64_t)gridDim.x * nwarps;
+  const int64_t gw = (int64_t)blockIdx.x * nwarps + warp;
+  if (lane == 0)
+    for (int s = 0; s < stages; ++s) {
+      const int64_t r = gw + s * NW;
+      if (r >= rows) break;
+      mbar_expect_tx(&bars[s], row_bytes);
+      bulk_load_1d(ring + (size_t)s * row_bytes, x + r * xs, row_bytes, &bars[s]);
+    }
+  const float invC = 1.0f / (float)C;
+  int64_t j = 0;
+  bool ok = true;
+  for (int64_t r = gw; r < rows; r += NW, ++j) {
+    const int slot = (int)(j % stages);
+    const uint32_t parity = (uint32_t)((j / stages) & 1);
+    ok = __all_sync(0xffffffffu, mbar_wait(&bars[slot], parity, &abort_flag, status, kStreamSite));
+    if (!ok) break;
+    const Pack<T, VW>* src = reinterpret_cast<const Pack<T, VW>*>(ring + (size_t)slot * row_bytes);
+    float mu = 0.f, rs;
+    if (LAYER) {
+      // Shifted-data variance with K = the row's first element (see norm_fwd_kernel).
+      const float K = Cvt<T>::to_f(src[0].v[0]);
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll 4
+      for (int v = lane; v < nv; v += 32) {
+        float xv[VW];
+        const Pack<T, VW> pk = src[v];  // one 16-byte shared load
+        unpack_vec<T, VW>(pk, xv);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) {
+          const float d = xv[e] - K;
+          s1 += d;
+          s2 = fmaf(d, d, s2);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+      const float d1 = s1 * invC;
+      mu = K + d1;
+      rs = 1.0f / sqrtf(fmaxf(s2 * invC - d1 * d1, 0.f) + eps);
+    } else {
+      float ss = 0.f;
+#pragma unroll 4
+      for (int v = lane; v < nv; v += 32) {
+        float xv[VW];
+        const Pack<T, VW> pk = src[v];  // one 16-byte shared load
+        unpack_vec<T, VW>(pk, xv);
+#pragma unroll
+        for (int e = 0; e < VW; ++e) ss = fmaf(xv[e], xv[e], ss);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      rs = 1.0f / sqrtf(ss * invC + eps);
+    }
+    T* dst = y + r * ys;
+#pragma unroll 4
+    for (int v = lane; v < nv; v += 32) {
+      float xv[VW], out[VW], wv[VW], bv[VW];
+      const Pack<T, VW> pk = src[v];
+      unpack_vec<T, VW>(pk, xv);
+      load_params<VW>(params, nv, v, wv);
+      if (LAYER) load_params<VW>(params + C, nv, v, bv);
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        const float t = (xv[e] - mu) * rs * wv[e];
+        out[e] = LAYER ? t + bv[e] : t;
+      }
+      store_vec<T, VW>(dst + (int64_t)v * VW, out);
+    }
+    if (lane == 0) {
+      if (rstd_out) rstd_out[r] = rs;
+      if (LAYER && mean_out) mean_out[r] = mu;
+    }
+    __syncwarp();
+    if (lane == 0) {
+      const int64_t rn = r + stages * NW;
+      if (rn < rows) {
+        fence_proxy_async_smem();  // this warp's reads of the slot precede the refill
+        mbar_expect_tx(&bars[slot], row_bytes);
+        bulk_load_1d(ring + (size_t)slot * row_bytes, x + rn * xs, row_bytes, &bars[slot]);
+      }
+    }
+  }
+  if (!ok && lane == 0) {
+    // Copies issued for rows j .. j + stages - 1 may still be in flight.
+    for (int64_t k = j; k < j + stages; ++k) {
+      if (gw + k * NW >= rows) break;
+      if (!bar_wait_drain(&bars[k % stages], (uint32_t)((k / stages) & 1))) break;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ backward
 // g = dy * w, xhat = (x - mu) * r
 //   rmsnorm:   dx = r * (g - xhat * mean(g * xhat))
@@ -297,6 +462,185 @@ __global__ void __launch_bounds__(kBlock) norm_bwd_kernel(
         for (int e = 0; e < VW; ++e) {
           part_w[prow * C + (int64_t)vi * VW + e] = accw[i][e];
           if (LAYER && part_b) part_b[prow * C + (int64_t)vi * VW + e] = accb[i][e];
+        }
+    }
+  }
+}
+
+// ------------------------------------------------------ backward, streamed
+// Rows of 256..1024 16-byte vectors (C = 2048..8192 in 16-bit): one CTA of 256
+// threads per SM walks blocks of R consecutive rows (blocks blockIdx.x,
+// blockIdx.x + gridDim.x, ...).  x and dy of a block arrive in a shared-memory
+// ring slot by two 1-D bulk copies; thread t owns vectors t, t + 256, ... of every
+// row, so its dweight / dbias partials stay in registers for the whole kernel.
+// One barrier per block: warps publish their 2R row sums into a double-buffered
+// slot, and after the barrier every thread of the CTA has finished the previous
+// block, so thread 0 refills that block's ring slot.
+constexpr int kBwdStreamSite = 93;
+
+template <typename T, typename WT, int VPT, int R, bool LAYER>
+__global__ void __launch_bounds__(kBlock, 1) norm_bwd_stream_kernel(
+    const T* __restrict__ dy, const T* __restrict__ x, const void* __restrict__ w,
+    const float* __restrict__ mean_in, const float* __restrict__ rstd_in, T* __restrict__ dx,
+    float* __restrict__ part_w, float* __restrict__ part_b, int64_t rows, int C, int stages,
+    int* status) {
+  constexpr int VW = 16 / sizeof(T);
+  constexpr int NWARP = kBlock / 32;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __shared__ float red[2][NWARP][2 * R];
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = C / VW;
+  const uint32_t row_bytes = (uint32_t)C * sizeof(T);
+  const uint32_t slot_bytes = 2u * R * row_bytes;  // [R rows of x][R rows of dy]
+  float* params = reinterpret_cast<float*>(smem_raw);
+  const size_t poff = ((size_t)C * sizeof(float) + 127) & ~(size_t)127;
+  unsigned char* ring = smem_raw + poff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + (size_t)stages * slot_bytes);
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < stages; ++s) mbar_init(&bars[s], 1);
+    fence_mbar_init();
+  }
+  stage_params_planar<WT, VW>(params, w, nullptr, C, false);  // ends with __syncthreads
+
+  const int64_t nblocks = (rows + R - 1) / R;
+  auto issue = [&](int64_t blk, int slot) {
+    const int64_t r0 = blk * R;
+    const uint32_t n = (uint32_t)(rows - r0 < R ? rows - r0 : (int64_t)R) * row_bytes;
+    unsigned char* dst = ring + (size_t)slot * slot_bytes;
+    mbar_expect_tx(&bars[slot], 2 * n);
+    bulk_load_1d(dst, x + r0 * C, n, &bars[slot]);
+    bulk_load_1d(dst + (size_t)R * row_bytes, dy + r0 * C, n, &bars[slot]);
+  };
+  if (threadIdx.x == 0)
+    for (int s = 0; s < stages; ++s) {
+      const int64_t blk = blockIdx.x + (int64_t)s * gridDim.x;
+      if (blk >= nblocks) break;
+      issue(blk, s);
+    }
+
+  const float invC = 1.0f / (float)C;
+  float accw[VPT][VW], accb[VPT][VW];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i)
+#pragma unroll
+    for (int e = 0; e < VW; ++e) accw[i][e] = accb[i][e] = 0.f;
+
+  int64_t j = 0;
+  bool ok = true;
+  for (int64_t blk = blockIdx.x; blk < nblocks; blk += gridDim.x, ++j) {
+    const int slot = (int)(j % stages);
+    const int64_t r0 = blk * R;
+    float rs[R], mu[R];
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const bool live = r0 + k < rows;
+      rs[k] = live ? rstd_in[r0 + k] : 0.f;
+      mu[k] = (LAYER && live) ? mean_in[r0 + k] : 0.f;
+    }
+    ok = mbar_wait(&bars[slot], (uint32_t)((j / stages) & 1), &abort_flag, status, kBwdStreamSite);
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+    const unsigned char* sl = ring + (size_t)slot * slot_bytes;
+    float sums[2 * R];  // per row: sum(g), sum(g * xhat)
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const Pack<T, VW>* xr = reinterpret_cast<const Pack<T, VW>*>(sl + (size_t)k * row_bytes);
+      const Pack<T, VW>* dr = reinterpret_cast<const Pack<T, VW>*>(sl + (size_t)(R + k) * row_bytes);
+      const bool live = r0 + k < rows;
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int v = threadIdx.x + i * kBlock;
+        if (live && v < nv) {
+          float xx[VW], dd[VW], wp[VW];
+          const Pack<T, VW> px = xr[v], pd = dr[v];  // 16-byte shared loads
+          unpack_vec<T, VW>(px, xx);
+          unpack_vec<T, VW>(pd, dd);
+          load_params<VW>(params, nv, v, wp);
+#pragma unroll
+          for (int e = 0; e < VW; ++e) {
+            const float xh = (xx[e] - mu[k]) * rs[k];
+            const float gv = dd[e] * wp[e];
+            accw[i][e] = fmaf(dd[e], xh, accw[i][e]);
+            if (LAYER) accb[i][e] += dd[e];
+            s0 += gv;
+            s1 = fmaf(gv, xh, s1);
+          }
+        }
+      }
+      sums[2 * k] = s0;
+      sums[2 * k + 1] = s1;
+    }
+#pragma unroll
+    for (int q = 0; q < 2 * R; ++q)
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sums[q] += __shfl_xor_sync(0xffffffffu, sums[q], o);
+    const int buf = (int)(j & 1);
+    if (lane == 0)
+#pragma unroll
+      for (int q = 0; q < 2 * R; ++q) red[buf][warp][q] = sums[q];
+    __syncthreads();
+    // Every thread is past the previous block: its slot can be refilled.
+    if (threadIdx.x == 0 && j > 0) {
+      const int64_t nb = blk - gridDim.x + (int64_t)stages * gridDim.x;
+      if (nb < nblocks) {
+        fence_proxy_async_smem();
+        issue(nb, (int)((j - 1) % stages));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2 * R; ++q) {
+      float t = 0.f;
+#pragma unroll
+      for (int wv = 0; wv < NWARP; ++wv) t += red[buf][wv][q];
+      sums[q] = t;
+    }
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      if (r0 + k >= rows) break;
+      const Pack<T, VW>* xr = reinterpret_cast<const Pack<T, VW>*>(sl + (size_t)k * row_bytes);
+      const Pack<T, VW>* dr = reinterpret_cast<const Pack<T, VW>*>(sl + (size_t)(R + k) * row_bytes);
+      const float mg = LAYER ? sums[2 * k] * invC : 0.f;
+      const float mgx = sums[2 * k + 1] * invC;
+#pragma unroll
+      for (int i = 0; i < VPT; ++i) {
+        const int v = threadIdx.x + i * kBlock;
+        if (v < nv) {
+          float xx[VW], dd[VW], out[VW], wp[VW];
+          const Pack<T, VW> px = xr[v], pd = dr[v];
+          unpack_vec<T, VW>(px, xx);
+          unpack_vec<T, VW>(pd, dd);
+          load_params<VW>(params, nv, v, wp);
+#pragma unroll
+          for (int e = 0; e < VW; ++e) {
+            const float xh = (xx[e] - mu[k]) * rs[k];
+            out[e] = rs[k] * (dd[e] * wp[e] - mg - xh * mgx);
+          }
+          store_vec<T, VW>(dx + (r0 + k) * (int64_t)C + (int64_t)v * VW, out);
+        }
+      }
+    }
+  }
+  if (!ok) {
+    if (threadIdx.x == 0)  // copies for blocks j .. j + stages - 1 may still be in flight
+      for (int64_t k = j; k < j + stages; ++k) {
+        if (blockIdx.x + k * gridDim.x >= nblocks) break;
+        if (!bar_wait_drain(&bars[k % stages], (uint32_t)((k / stages) & 1))) break;
+      }
+    return;
+  }
+  if (part_w) {
+    const int64_t prow = blockIdx.x;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int v = threadIdx.x + i * kBlock;
+      if (v < nv)
+#pragma unroll
+        for (int e = 0; e < VW; ++e) {
+          part_w[prow * C + (int64_t)v * VW + e] = accw[i][e];
+          if (LAYER && part_b) part_b[prow * C + (int64_t)v * VW + e] = accb[i][e];
         }
     }
   }
@@ -407,6 +751,48 @@ int launch_fwd_vpt(Plan& p, cudaStream_t s, const void* x, int64_t xs, const voi
   return SCREE_OK;
 }
 
+// Streamed forward plan: 8 (else 4) warps with 3 (else 2) row slots each,
+// whatever fits next to the staged parameters; 0 stages = use norm_fwd_kernel.
+struct StreamPlan {
+  int warps, stages, smem, grid;
+};
+StreamPlan stream_plan(int64_t rows, int64_t C, int esize, bool aligned16, bool layer) {
+  StreamPlan sp{0, 0, 0, 0};
+  const int64_t row_bytes = C * esize;
+  if (!aligned16 || row_bytes % 16 != 0 || row_bytes < 1024 || row_bytes > 64 * 1024) return sp;
+  const int64_t params = ((C * 4 * (layer ? 2 : 1)) + 127) & ~int64_t(127);
+  const int64_t limit = 227 * 1024 - 64;  // opt-in maximum minus static shared memory
+  for (int warps : {8, 4})
+    for (int st : {3, 2}) {
+      const int64_t need = params + (int64_t)warps * st * (row_bytes + 8);
+      if (need <= limit && sp.stages == 0) {
+        sp.warps = warps;
+        sp.stages = st;
+        sp.smem = (int)need;
+      }
+    }
+  return sp;
+}
+
+template <typename T, typename WT, bool LAYER>
+int launch_fwd_stream(StreamPlan& sp, cudaStream_t s, const void* x, int64_t xs, const void* w,
+                      const void* b, void* y, int64_t ys, float* mean, float* rstd, int64_t rows,
+                      int C, float eps) {
+  auto kernel = norm_fwd_stream_kernel<T, WT, LAYER>;
+  if (sp.smem > 48 * 1024)
+    SCREE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sp.smem));
+  int occ = 0;
+  SCREE_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, sp.warps * 32, sp.smem));
+  occ = std::max(occ, 1);
+  const int64_t need = (rows + sp.warps - 1) / sp.warps;
+  sp.grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)occ * num_sms()));
+  ProfScope prof(PROF_NORM_FWD, s);
+  kernel<<<sp.grid, sp.warps * 32, sp.smem, s>>>((const T*)x, xs, w, b, (T*)y, ys, mean, rstd,
+                                                 rows, C, sp.stages, eps, device_status_ptr());
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
 template <typename T, typename WT, bool LAYER>
 int launch_fwd(Plan& p, cudaStream_t s, const void* x, int64_t xs, const void* w,
                const void* b, void* y, int64_t ys, float* mean, float* rstd, int64_t rows, int C,
@@ -439,6 +825,60 @@ int launch_bwd(Plan& p, cudaStream_t s, const void* dy, const void* x, const voi
                int64_t rows, int C) {
   if (p.vw == 1) return launch_bwd_vpt<T, WT, 1, LAYER>(p, s, dy, x, w, mean, rstd, dx, pw, pb, rows, C);
   return launch_bwd_vpt<T, WT, 16 / sizeof(T), LAYER>(p, s, dy, x, w, mean, rstd, dx, pw, pb, rows, C);
+}
+
+// Streamed backward plan: R rows per block so a ring slot (x and dy) is about
+// 64 KB, as many slots (3..8) as fit next to the staged weight; 0 stages = use
+// norm_bwd_kernel.
+struct BwdStreamPlan {
+  int vpt, R, stages, smem, grid;
+};
+BwdStreamPlan bwd_stream_plan(int64_t rows, int64_t C, int esize, bool aligned16) {
+  BwdStreamPlan sp{0, 0, 0, 0, 0};
+  const int64_t row_bytes = C * esize;
+  if (!aligned16 || row_bytes % 16 != 0) return sp;
+  const int64_t nv = row_bytes / 16;
+  if (nv < 256 || nv > 4 * kBlock) return sp;
+  sp.vpt = nv <= kBlock ? 1 : (nv <= 2 * kBlock ? 2 : 4);
+  sp.R = row_bytes <= 8192 ? 4 : (row_bytes <= 16384 ? 2 : 1);
+  const int64_t slot = 2 * sp.R * row_bytes;
+  const int64_t params = (C * 4 + 127) & ~int64_t(127);
+  const int64_t limit = 227 * 1024 - 1024;  // opt-in maximum minus static shared memory
+  const int64_t st = std::min<int64_t>(8, (limit - params) / (slot + 8));
+  if (st < 3) return BwdStreamPlan{0, 0, 0, 0, 0};
+  sp.stages = (int)st;
+  sp.smem = (int)(params + st * slot + st * 8);
+  const int64_t nblocks = (rows + sp.R - 1) / sp.R;
+  sp.grid = (int)std::max<int64_t>(1, std::min<int64_t>(nblocks, num_sms()));
+  return sp;
+}
+
+template <typename T, typename WT, int VPT, int R, bool LAYER>
+int launch_bwd_stream_r(const BwdStreamPlan& sp, cudaStream_t s, const void* dy, const void* x,
+                        const void* w, const float* mean, const float* rstd, void* dx, float* pw,
+                        float* pb, int64_t rows, int C) {
+  auto kernel = norm_bwd_stream_kernel<T, WT, VPT, R, LAYER>;
+  SCREE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sp.smem));
+  ProfScope prof(PROF_NORM_BWD, s);
+  kernel<<<sp.grid, kBlock, sp.smem, s>>>((const T*)dy, (const T*)x, w, mean, rstd, (T*)dx, pw, pb,
+                                          rows, C, sp.stages, device_status_ptr());
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+template <typename T, typename WT, bool LAYER>
+int launch_bwd_stream(const BwdStreamPlan& sp, cudaStream_t s, const void* dy, const void* x,
+                      const void* w, const float* mean, const float* rstd, void* dx, float* pw,
+                      float* pb, int64_t rows, int C) {
+#define SCREE_BS(V, RR) \
+  if (sp.vpt == V && sp.R == RR) \
+    return launch_bwd_stream_r<T, WT, V, RR, LAYER>(sp, s, dy, x, w, mean, rstd, dx, pw, pb, rows, C)
+  SCREE_BS(1, 4); SCREE_BS(1, 2); SCREE_BS(1, 1);
+  SCREE_BS(2, 4); SCREE_BS(2, 2); SCREE_BS(2, 1);
+  SCREE_BS(4, 4); SCREE_BS(4, 2); SCREE_BS(4, 1);
+#undef SCREE_BS
+  set_last_error("norm bwd: no streamed variant for vpt=%d R=%d", sp.vpt, sp.R);
+  return SCREE_ERR_INVALID;
 }
 
 // Dispatch over (x dtype, weight dtype).
@@ -480,11 +920,14 @@ int norm_fwd(const void* x, int64_t xs, const void* w, const void* b, int w_dtyp
     return SCREE_ERR_UNSUPPORTED;
   }
   if (!w) w_dtype = dtype;
+  StreamPlan sp = stream_plan(rows, C, es, a16, LAYER);
   SCREE_BIND_DEVICE(stream, x);
   cudaStream_t s = (cudaStream_t)stream;
   return dispatch_types<LAYER>(dtype, w_dtype, [&](auto* tp, auto* wp) {
     using T = std::remove_pointer_t<decltype(tp)>;
     using WT = std::remove_pointer_t<decltype(wp)>;
+    if (sp.stages > 0)
+      return launch_fwd_stream<T, WT, LAYER>(sp, s, x, xs, w, b, y, ys, mean, rstd, rows, (int)C, eps);
     return launch_fwd<T, WT, LAYER>(p, s, x, xs, w, b, y, ys, mean, rstd, rows, (int)C, eps);
   });
 }
@@ -525,9 +968,11 @@ int norm_bwd(const void* dy, const void* x, const void* w, int w_dtype, const fl
     set_last_error("norm bwd: feature dim %lld too large", (long long)C);
     return SCREE_ERR_UNSUPPORTED;
   }
-  // Partial rows: one per row group of the planned grid (the launch may use
-  // fewer CTAs, then fewer rows are written and reduced).
-  const int64_t P = (int64_t)p.grid * (kBlock / p.tpr);
+  const BwdStreamPlan sp = bwd_stream_plan(rows, C, es, a16);
+  // Partial rows: one per CTA of the streamed kernel, else one per row group of
+  // the planned grid (the launch may use fewer CTAs, then fewer rows are written
+  // and reduced).  Both fit the workspace of scree_norm_bwd_workspace_size.
+  const int64_t P = sp.stages ? (int64_t)sp.grid : (int64_t)p.grid * (kBlock / p.tpr);
   float* pw = nullptr;
   float* pb = nullptr;
   if (want_w || want_b) {
@@ -541,16 +986,18 @@ int norm_bwd(const void* dy, const void* x, const void* w, int w_dtype, const fl
   int rc = dispatch_types<LAYER>(dtype, w_dtype, [&](auto* tp, auto* wp) {
     using T = std::remove_pointer_t<decltype(tp)>;
     using WT = std::remove_pointer_t<decltype(wp)>;
+    if (sp.stages)
+      return launch_bwd_stream<T, WT, LAYER>(sp, s, dy, x, w, mean, rstd, dx, pw, pb, rows, (int)C);
     return launch_bwd<T, WT, LAYER>(p, s, dy, x, w, mean, rstd, dx, pw, pb, rows, (int)C);
   });
   if (rc != SCREE_OK) return rc;
   const unsigned cgrid = (unsigned)((C + 31) / 32);
   if (want_w) {
-    column_sum_kernel<<<cgrid, 256, 0, s>>>(pw, (int64_t)p.grid * (kBlock / p.tpr), (int)C, dw);
+    column_sum_kernel<<<cgrid, 256, 0, s>>>(pw, P, (int)C, dw);
     SCREE_LAUNCH_CHECK();
   }
   if (want_b) {
-    column_sum_kernel<<<cgrid, 256, 0, s>>>(pb, (int64_t)p.grid * (kBlock / p.tpr), (int)C, db);
+    column_sum_kernel<<<cgrid, 256, 0, s>>>(pb, P, (int)C, db);
     SCREE_LAUNCH_CHECK();
   }
   return SCREE_OK;

@@ -124,6 +124,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+// 1-D bulk copy global -> shared (no tensor map, no multicast): `bytes` and
+// both addresses multiples of 16; completion counted on `bar` as tx bytes.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // 3-D tiled reduce-add of a shared-memory box into global memory (bulk group).
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* m, const void* src, int c0,
                                                   int c1, int c2) {

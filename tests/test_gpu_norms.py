@@ -42,6 +42,9 @@ CASES = [
     (257, 100, torch.float32),    # vectorised, odd row count
     (129, 33, torch.float16),     # scalar path (C*2 bytes not a multiple of 16)
     (64, 8192, torch.bfloat16),
+    (333, 2048, torch.bfloat16),    # streamed kernels, last row block ragged
+    (500, 2048, torch.float32),     # streamed kernels, 32-bit rows
+    (5, 4096, torch.float16),       # fewer rows than SMs
     (1, 8, torch.float32),
 ]
 
@@ -130,6 +133,13 @@ def test_norm_multidim_and_strided(cuda):
     view = wide[:, :256]
     y = varlen_rmsnorm_triton(view, None, 1e-6)
     _assert_close(y, oracle.rmsnorm_fwd(to64(view), None, 1e-6), torch.float16)
+    wide = torch.randn((40, 2048), device=cuda, dtype=torch.bfloat16)
+    view = wide[:, :1024]  # 2 KB rows 4 KB apart: streamed forward with a row stride
+    w = torch.rand(1024, device=cuda) + 0.5
+    b = torch.randn(1024, device=cuda) * 0.1
+    from scree_b200.kernels.native import varlen_layernorm_triton
+    y = varlen_layernorm_triton(view, w, b, 1e-5)
+    _assert_close(y, oracle.layernorm_fwd(to64(view), to64(w), to64(b), 1e-5), torch.bfloat16)
 
 
 def test_array_level_norms(cuda):
