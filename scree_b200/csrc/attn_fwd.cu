@@ -349,6 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < BN / 32; ++c)
         tmem_ld32(col_s + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
       tmem_wait_ld();
+#ifdef SCREE_TRACE
+      const long long t_ld = clock64();
+      SCREE_TRACE_ADD(22, t_ld - t_sm0);
+#endif
       const int k0 = j * BN;
       const bool need_mask = (k0 + BN > L) || (CAUSAL && k0 + BN - 1 > qt0);
       if (need_mask) {
@@ -368,6 +372,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
                              fmaxf(mx8[6], mx8[7]));
       const float m_cand = mx * sl2;
+#ifdef SCREE_TRACE
+      const long long t_mx = clock64();
+      SCREE_TRACE_ADD(23, t_mx - t_ld);
+#endif
       float alpha = 1.f;
       bool need = false;
       if (m_used == -INFINITY) {
@@ -398,6 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float ra, rb;
       f2_unpack(f2_add(f2_add(rs4[0], rs4[1]), f2_add(rs4[2], rs4[3])), ra, rb);
       const float rs = ra + rb;
+#ifdef SCREE_TRACE
+      const long long t_ex = clock64();
+      SCREE_TRACE_ADD(24, t_ex - t_mx);
+#endif
       if (j >= 1) {
         // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
         // before P_X(j) overwrites the columns it read.  It already is in the
@@ -418,6 +430,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       l = l * alpha + rs;
+#ifdef SCREE_TRACE
+      const long long t_rs = clock64();
+      SCREE_TRACE_ADD(25, t_rs - t_ex);
+#endif
       tmem_st32u(col_s, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
       tmem_st32u(col_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
       tmem_wait_st();

@@ -231,6 +231,30 @@ __device__ __forceinline__ void load_params(const float* planes, int nv, int v, 
   }
 }
 
+// Warp sums of N values at once (N a power of two, <= 32) by recursive halving:
+// at each step a lane keeps one half of its values and sends the other half to
+// its partner, so N values cost N - 1 + log2(32 / N) shuffles instead of
+// 5 N.  Returns the warp-wide sum of value (lane >> (5 - log2 N)).
+template <int N>
+__device__ __forceinline__ float warp_sum_multi(float (&v)[N], int lane) {
+  static_assert(N >= 1 && N <= 32 && (N & (N - 1)) == 0, "N must be a power of two <= 32");
+  int off = 16;
+#pragma unroll
+  for (int cnt = N; cnt > 1; cnt >>= 1, off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int i = 0; i < cnt / 2; ++i) {
+      const float send = upper ? v[i] : v[i + cnt / 2];
+      const float keep = upper ? v[i + cnt / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+    }
+  }
+  float t = v[0];
+#pragma unroll
+  for (; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+  return t;
+}
+
 // ------------------------------------------------------- forward, streamed
 // Rows of at least 1 KB (C = 4096 in 16-bit is 8 KB): every warp owns whole rows
 // (rows warp_id, warp_id + all_warps, ...) and a private ring of `stages` row
@@ -468,9 +492,9 @@ __global__ void __launch_bounds__(kBlock) norm_bwd_kernel(
 }
 
 // ------------------------------------------------------ backward, streamed
-// Rows of 256..1024 16-byte vectors (C = 2048..8192 in 16-bit): one CTA of 256
-// threads per SM walks blocks of R consecutive rows (blocks blockIdx.x,
-// blockIdx.x + gridDim.x, ...).  x and dy of a block arrive in a shared-memory
+// Rows of 256..1024 16-byte vectors (C = 2048..8192 in 16-bit): one CTA of NT
+// (256, or 512 for rows of at least 512 vectors) threads per SM walks blocks of
+// R consecutive rows (blocks blockIdx.x, blockIdx.x + gridDim.x, ...).  x and dy of a block arrive in a shared-memory
 // ring slot by two 1-D bulk copies; thread t owns vectors t, t + 256, ... of every
 // row, so its dweight / dbias partials stay in registers for the whole kernel.
 // One barrier per block: warps publish their 2R row sums into a double-buffered
@@ -478,14 +502,14 @@ __global__ void __launch_bounds__(kBlock) norm_bwd_kernel(
 // block, so thread 0 refills that block's ring slot.
 constexpr int kBwdStreamSite = 93;
 
-template <typename T, typename WT, int VPT, int R, bool LAYER>
-__global__ void __launch_bounds__(kBlock, 1) norm_bwd_stream_kernel(
+template <typename T, typename WT, int NT, int VPT, int R, bool LAYER>
+__global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
     const T* __restrict__ dy, const T* __restrict__ x, const void* __restrict__ w,
     const float* __restrict__ mean_in, const float* __restrict__ rstd_in, T* __restrict__ dx,
     float* __restrict__ part_w, float* __restrict__ part_b, int64_t rows, int C, int stages,
     int* status) {
   constexpr int VW = 16 / sizeof(T);
-  constexpr int NWARP = kBlock / 32;
+  constexpr int NWARP = NT / 32;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __shared__ float red[2][NWARP][2 * R];
   __shared__ int abort_flag;
@@ -552,7 +576,7 @@ __global__ void __launch_bounds__(kBlock, 1) norm_bwd_stream_kernel(
       float s0 = 0.f, s1 = 0.f;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
-        const int v = threadIdx.x + i * kBlock;
+        const int v = threadIdx.x + i * NT;
         if (live && v < nv) {
           float xx[VW], dd[VW], wp[VW];
           const Pack<T, VW> px = xr[v], pd = dr[v];  // 16-byte shared loads
@@ -573,14 +597,12 @@ __global__ void __launch_bounds__(kBlock, 1) norm_bwd_stream_kernel(
       sums[2 * k] = s0;
       sums[2 * k + 1] = s1;
     }
-#pragma unroll
-    for (int q = 0; q < 2 * R; ++q)
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sums[q] += __shfl_xor_sync(0xffffffffu, sums[q], o);
+    constexpr int Q2 = 2 * R, LPQ = 32 / Q2;  // lanes per row sum
     const int buf = (int)(j & 1);
-    if (lane == 0)
-#pragma unroll
-      for (int q = 0; q < 2 * R; ++q) red[buf][warp][q] = sums[q];
+    {
+      const float t = warp_sum_multi<Q2>(sums, lane);  // sum #(lane / LPQ)
+      if (lane % LPQ == 0) red[buf][warp][lane / LPQ] = t;
+    }
     __syncthreads();
     // Every thread is past the previous block: its slot can be refilled.
     if (threadIdx.x == 0 && j > 0) {
@@ -590,12 +612,16 @@ __global__ void __launch_bounds__(kBlock, 1) norm_bwd_stream_kernel(
         issue(nb, (int)((j - 1) % stages));
       }
     }
-#pragma unroll
-    for (int q = 0; q < 2 * R; ++q) {
+    {
+      // Lanes split the (sum, warp) pairs, reduce, and broadcast the totals.
+      const int q = lane / LPQ, g = lane % LPQ;
       float t = 0.f;
 #pragma unroll
-      for (int wv = 0; wv < NWARP; ++wv) t += red[buf][wv][q];
-      sums[q] = t;
+      for (int wv = g; wv < NWARP; wv += LPQ) t += red[buf][wv][q];
+#pragma unroll
+      for (int o = LPQ / 2; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+#pragma unroll
+      for (int qq = 0; qq < Q2; ++qq) sums[qq] = __shfl_sync(0xffffffffu, t, qq * LPQ);
     }
 #pragma unroll
     for (int k = 0; k < R; ++k) {
@@ -606,7 +632,7 @@ __global__ void __launch_bounds__(kBlock, 1) norm_bwd_stream_kernel(
       const float mgx = sums[2 * k + 1] * invC;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
-        const int v = threadIdx.x + i * kBlock;
+        const int v = threadIdx.x + i * NT;
         if (v < nv) {
           float xx[VW], dd[VW], out[VW], wp[VW];
           const Pack<T, VW> px = xr[v], pd = dr[v];
@@ -635,7 +661,7 @@ __global__ void __launch_bounds__(kBlock, 1) norm_bwd_stream_kernel(
     const int64_t prow = blockIdx.x;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      const int v = threadIdx.x + i * kBlock;
+      const int v = threadIdx.x + i * NT;
       if (v < nv)
 #pragma unroll
         for (int e = 0; e < VW; ++e) {
@@ -831,21 +857,25 @@ int launch_bwd(Plan& p, cudaStream_t s, const void* dy, const void* x, const voi
 // 64 KB, as many slots (3..8) as fit next to the staged weight; 0 stages = use
 // norm_bwd_kernel.
 struct BwdStreamPlan {
-  int vpt, R, stages, smem, grid;
+  int nt, vpt, R, stages, smem, grid;
 };
-BwdStreamPlan bwd_stream_plan(int64_t rows, int64_t C, int esize, bool aligned16) {
-  BwdStreamPlan sp{0, 0, 0, 0, 0};
+BwdStreamPlan bwd_stream_plan(int64_t rows, int64_t C, int esize, bool aligned16, bool layer) {
+  BwdStreamPlan sp{0, 0, 0, 0, 0, 0};
   const int64_t row_bytes = C * esize;
   if (!aligned16 || row_bytes % 16 != 0) return sp;
   const int64_t nv = row_bytes / 16;
   if (nv < 256 || nv > 4 * kBlock) return sp;
-  sp.vpt = nv <= kBlock ? 1 : (nv <= 2 * kBlock ? 2 : 4);
+  // 512 threads (one vector per thread per row) measured faster for RMSNorm at
+  // C = 4096; LayerNorm's extra dbias partials keep it at 256.
+  sp.nt = (!layer && nv >= 2 * kBlock) ? 2 * kBlock : kBlock;
+  sp.vpt = (int)((nv + sp.nt - 1) / sp.nt);
+  if (sp.vpt == 3) sp.vpt = 4;
   sp.R = row_bytes <= 8192 ? 4 : (row_bytes <= 16384 ? 2 : 1);
   const int64_t slot = 2 * sp.R * row_bytes;
   const int64_t params = (C * 4 + 127) & ~int64_t(127);
   const int64_t limit = 227 * 1024 - 1024;  // opt-in maximum minus static shared memory
   const int64_t st = std::min<int64_t>(8, (limit - params) / (slot + 8));
-  if (st < 3) return BwdStreamPlan{0, 0, 0, 0, 0};
+  if (st < 3) return BwdStreamPlan{0, 0, 0, 0, 0, 0};
   sp.stages = (int)st;
   sp.smem = (int)(params + st * slot + st * 8);
   const int64_t nblocks = (rows + sp.R - 1) / sp.R;
@@ -853,15 +883,15 @@ BwdStreamPlan bwd_stream_plan(int64_t rows, int64_t C, int esize, bool aligned16
   return sp;
 }
 
-template <typename T, typename WT, int VPT, int R, bool LAYER>
+template <typename T, typename WT, int NT, int VPT, int R, bool LAYER>
 int launch_bwd_stream_r(const BwdStreamPlan& sp, cudaStream_t s, const void* dy, const void* x,
                         const void* w, const float* mean, const float* rstd, void* dx, float* pw,
                         float* pb, int64_t rows, int C) {
-  auto kernel = norm_bwd_stream_kernel<T, WT, VPT, R, LAYER>;
+  auto kernel = norm_bwd_stream_kernel<T, WT, NT, VPT, R, LAYER>;
   SCREE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sp.smem));
   ProfScope prof(PROF_NORM_BWD, s);
-  kernel<<<sp.grid, kBlock, sp.smem, s>>>((const T*)dy, (const T*)x, w, mean, rstd, (T*)dx, pw, pb,
-                                          rows, C, sp.stages, device_status_ptr());
+  kernel<<<sp.grid, NT, sp.smem, s>>>((const T*)dy, (const T*)x, w, mean, rstd, (T*)dx, pw, pb,
+                                      rows, C, sp.stages, device_status_ptr());
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
@@ -870,14 +900,19 @@ template <typename T, typename WT, bool LAYER>
 int launch_bwd_stream(const BwdStreamPlan& sp, cudaStream_t s, const void* dy, const void* x,
                       const void* w, const float* mean, const float* rstd, void* dx, float* pw,
                       float* pb, int64_t rows, int C) {
-#define SCREE_BS(V, RR) \
-  if (sp.vpt == V && sp.R == RR) \
-    return launch_bwd_stream_r<T, WT, V, RR, LAYER>(sp, s, dy, x, w, mean, rstd, dx, pw, pb, rows, C)
-  SCREE_BS(1, 4); SCREE_BS(1, 2); SCREE_BS(1, 1);
-  SCREE_BS(2, 4); SCREE_BS(2, 2); SCREE_BS(2, 1);
-  SCREE_BS(4, 4); SCREE_BS(4, 2); SCREE_BS(4, 1);
+#define SCREE_BS(NTV, V, RR)                                                                  \
+  if (sp.nt == NTV && sp.vpt == V && sp.R == RR)                                               \
+  return launch_bwd_stream_r<T, WT, NTV, V, RR, LAYER>(sp, s, dy, x, w, mean, rstd, dx, pw, pb, \
+                                                        rows, C)
+  // The combinations stream_plan can produce (16-byte vectors per row nv,
+  // 256..1024): 256 threads with nv <= 256 / 512 / 1024, and for RMSNorm 512
+  // threads with nv = 512 / up to 1024; R follows from the row size.
+  SCREE_BS(kBlock, 1, 4); SCREE_BS(kBlock, 2, 4); SCREE_BS(kBlock, 4, 2);
+  if constexpr (!LAYER) {
+    SCREE_BS(2 * kBlock, 1, 4); SCREE_BS(2 * kBlock, 2, 2);
+  }
 #undef SCREE_BS
-  set_last_error("norm bwd: no streamed variant for vpt=%d R=%d", sp.vpt, sp.R);
+  set_last_error("norm bwd: no streamed variant for nt=%d vpt=%d R=%d", sp.nt, sp.vpt, sp.R);
   return SCREE_ERR_INVALID;
 }
 
@@ -968,7 +1003,7 @@ int norm_bwd(const void* dy, const void* x, const void* w, int w_dtype, const fl
     set_last_error("norm bwd: feature dim %lld too large", (long long)C);
     return SCREE_ERR_UNSUPPORTED;
   }
-  const BwdStreamPlan sp = bwd_stream_plan(rows, C, es, a16);
+  const BwdStreamPlan sp = bwd_stream_plan(rows, C, es, a16, LAYER);
   // Partial rows: one per CTA of the streamed kernel, else one per row group of
   // the planned grid (the launch may use fewer CTAs, then fewer rows are written
   // and reduced).  Both fit the workspace of scree_norm_bwd_workspace_size.
