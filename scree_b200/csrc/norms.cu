@@ -319,7 +319,9 @@ __global__ void __launch_bounds__(kBlock) norm_fwd_stream_kernel(
     if (LAYER) {
       // Shifted-data variance with K = the row's first element (see norm_fwd_kernel).
       const float K = Cvt<T>::to_f(src[0].v[0]);
-      float s1 = 0.f, s2 = 0.f;
+      float a1[VW], a2[VW];  // one accumulator per vector element: short chains
+#pragma unroll
+      for (int e = 0; e < VW; ++e) a1[e] = a2[e] = 0.f;
 #pragma unroll 4
       for (int v = lane; v < nv; v += 32) {
         float xv[VW];
@@ -328,9 +330,15 @@ __global__ void __launch_bounds__(kBlock) norm_fwd_stream_kernel(
 #pragma unroll
         for (int e = 0; e < VW; ++e) {
           const float d = xv[e] - K;
-          s1 += d;
-          s2 = fmaf(d, d, s2);
+          a1[e] += d;
+          a2[e] = fmaf(d, d, a2[e]);
         }
+      }
+      float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        s1 += a1[e];
+        s2 += a2[e];
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -341,15 +349,20 @@ __global__ void __launch_bounds__(kBlock) norm_fwd_stream_kernel(
       mu = K + d1;
       rs = 1.0f / sqrtf(fmaxf(s2 * invC - d1 * d1, 0.f) + eps);
     } else {
-      float ss = 0.f;
+      float a2[VW];
+#pragma unroll
+      for (int e = 0; e < VW; ++e) a2[e] = 0.f;
 #pragma unroll 4
       for (int v = lane; v < nv; v += 32) {
         float xv[VW];
         const Pack<T, VW> pk = src[v];  // one 16-byte shared load
         unpack_vec<T, VW>(pk, xv);
 #pragma unroll
-        for (int e = 0; e < VW; ++e) ss = fmaf(xv[e], xv[e], ss);
+        for (int e = 0; e < VW; ++e) a2[e] = fmaf(xv[e], xv[e], a2[e]);
       }
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) ss += a2[e];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       rs = 1.0f / sqrtf(ss * invC + eps);
