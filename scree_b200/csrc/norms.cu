@@ -275,7 +275,7 @@ __device__ __forceinline__ bool bar_wait_drain(uint64_t* bar, uint32_t parity) {
 }
 
 template <typename T, typename WT, bool LAYER>
-__global__ void __launch_bounds__(kBlock) norm_fwd_stream_kernel(
+__global__ void __launch_bounds__(2 * kBlock) norm_fwd_stream_kernel(
     const T* __restrict__ x, int64_t xs, const void* __restrict__ w,
     const void* __restrict__ bias, T* __restrict__ y, int64_t ys, float* __restrict__ mean_out,
     float* __restrict__ rstd_out, int64_t rows, int C, int stages, float eps, int* status) {
@@ -790,7 +790,7 @@ int launch_fwd_vpt(Plan& p, cudaStream_t s, const void* x, int64_t xs, const voi
   return SCREE_OK;
 }
 
-// Streamed forward plan: 8 (else 4) warps with 3 (else 2) row slots each,
+// Streamed forward plan: 12, 8 or 4 warps with 2 or 3 row slots each,
 // whatever fits next to the staged parameters; 0 stages = use norm_fwd_kernel.
 struct StreamPlan {
   int warps, stages, smem, grid;
@@ -801,15 +801,17 @@ StreamPlan stream_plan(int64_t rows, int64_t C, int esize, bool aligned16, bool 
   if (!aligned16 || row_bytes % 16 != 0 || row_bytes < 1024 || row_bytes > 64 * 1024) return sp;
   const int64_t params = ((C * 4 * (layer ? 2 : 1)) + 127) & ~int64_t(127);
   const int64_t limit = 227 * 1024 - 64;  // opt-in maximum minus static shared memory
-  for (int warps : {8, 4})
-    for (int st : {3, 2}) {
-      const int64_t need = params + (int64_t)warps * st * (row_bytes + 8);
-      if (need <= limit && sp.stages == 0) {
-        sp.warps = warps;
-        sp.stages = st;
-        sp.smem = (int)need;
-      }
+  // (warps, row slots) in order of preference: 12 x 2 measured faster than 8 x 3
+  // for RMSNorm at C = 4096 (more warps, same shared memory), equal for LayerNorm.
+  const int cand[5][2] = {{12, 2}, {8, 3}, {8, 2}, {4, 3}, {4, 2}};
+  for (const auto& c : cand) {
+    const int64_t need = params + (int64_t)c[0] * c[1] * (row_bytes + 8);
+    if (need <= limit && sp.stages == 0) {
+      sp.warps = c[0];
+      sp.stages = c[1];
+      sp.smem = (int)need;
     }
+  }
   return sp;
 }
 
