@@ -108,11 +108,6 @@ __device__ __forceinline__ uint64_t mnmaj(uint32_t base, int rows, int kk) {
   return make_sdesc(base + kk * 16 * C::SWB, rows * C::SWB, 8 * C::SWB, C::SWZ);
 }
 // P^T / dS^T tile [BN keys][BQ queries], 64-query 128B-swizzled column blocks.
-// K-major view with K = queries:
-__device__ __forceinline__ uint64_t pt_kmaj(uint32_t base, int kk) {
-  const int e = kk * 16;
-  return make_sdesc(base + (e / 64) * BN * 128 + (e % 64) * 2, 16, 1024, SW_128B);
-}
 // MN-major view with K = keys (16 rows per step), MN = queries:
 __device__ __forceinline__ uint64_t pt_mnmaj(uint32_t base, int kk) {
   return make_sdesc(base + kk * 16 * 128, BN * 128, 1024, SW_128B);

@@ -711,7 +711,6 @@ struct Plan {
   int tpr;  // threads per row
   int vpt;  // vectors per thread
   int grid;
-  int rows_per_iter;  // forward: rows a row group loads before reducing (1 or 2)
   int smem;           // dynamic shared memory: staged weight (and bias)
   bool ok;
 };
@@ -744,7 +743,6 @@ Plan plan_for(int64_t rows, int64_t C, int esize, bool aligned16, int max_vpt, b
   // Grids measured best at cfg3 (hidden 4096): 4 CTAs per SM forward, 2 backward
   // (fewer dweight partial rows); launches also cap at the real occupancy.
   const int64_t cap = (int64_t)num_sms() * (bwd ? 2 : 4);
-  p.rows_per_iter = 1;
   // Staged parameters: weight (+ bias in the layernorm forward, sized for both).
   p.smem = (int)(C * sizeof(float) * (bwd ? 1 : 2));
   if (p.smem > 200 * 1024) p.ok = false;
@@ -771,12 +769,8 @@ int launch_fwd_vpt(Plan& p, cudaStream_t s, const void* x, int64_t xs, const voi
                    const void* b, void* y, int64_t ys, float* mean, float* rstd, int64_t rows,
                    int C, float eps) {
 #define SCREE_FWD(V)                                                                        \
-  if (p.rows_per_iter == 1)                                                                 \
-    launch_smem(norm_fwd_kernel<T, WT, VW, V, LAYER, 1>, p, s,                              \
-        (const T*)x, xs, w, b, (T*)y, ys, mean, rstd, rows, C, p.tpr, eps);                 \
-  else                                                                                      \
-    launch_smem(norm_fwd_kernel<T, WT, VW, V, LAYER, 2>, p, s,                              \
-        (const T*)x, xs, w, b, (T*)y, ys, mean, rstd, rows, C, p.tpr, eps)
+  launch_smem(norm_fwd_kernel<T, WT, VW, V, LAYER, 1>, p, s,                                \
+      (const T*)x, xs, w, b, (T*)y, ys, mean, rstd, rows, C, p.tpr, eps)
   ProfScope prof(PROF_NORM_FWD, s);
   switch (p.vpt) {
     case 1: SCREE_FWD(1); break;
@@ -881,7 +875,8 @@ BwdStreamPlan bwd_stream_plan(int64_t rows, int64_t C, int esize, bool aligned16
   const int64_t nv = row_bytes / 16;
   if (nv < 256 || nv > 4 * kBlock) return sp;
   // 512 threads (one vector per thread per row) measured faster for RMSNorm at
-  // C = 4096; LayerNorm's extra dbias partials keep it at 256.
+  // C = 4096; for LayerNorm (extra dbias partials, so 2 rows per block at 512
+  // threads) 256 threads measured faster.
   sp.nt = (!layer && nv >= 2 * kBlock) ? 2 * kBlock : kBlock;
   sp.vpt = (int)((nv + sp.nt - 1) / sp.nt);
   if (sp.vpt == 3) sp.vpt = 4;
