@@ -171,7 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = v_empty + C::VSTAGES;      // [2] per tile X
   uint64_t* p_full = s_full + 2;                // [2]
   uint64_t* pv_done = p_full + 2;               // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* p_half = pv_done + 2;               // [2] first half of P_X (keys 0..BN/2)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_half + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -196,6 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 128);
+      mbar_init(&p_half[x], 128);
       mbar_init(&pv_done[x], 1);
     }
     *abort_flag = 0;
@@ -269,16 +271,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                       kk > 0 ? 1u : 0u);
         umma_commit(&s_full[x]);
       };
-      auto issue_pv = [&](int x, int j) {
+      // O_X += P_X(j) V_j over keys [16 kk0, 16 kk1): the first half can run
+      // while the softmax warps are still forming the second.
+      auto issue_pv = [&](int x, int j, int kk0, int kk1) {
         const uint32_t vb = sV + (j % C::VSTAGES) * C::KV_BYTES;
         const uint32_t pt = tmem + C::COL_S + x * BN;
         const uint64_t dv = v_desc<D>(vb, 0);
         const uint32_t dt = tmem + C::COL_O + x * D;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys = 8 packed TMEM columns per step
+        for (int kk = kk0; kk < kk1; ++kk)  // 16 keys = 8 packed TMEM columns per step
           umma_f16_ts(dt, pt + kk * 8, dv + (uint32_t)((kk * 16 * C::SWB) >> 4), IDESC_O,
                       (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&pv_done[x]);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 4);
       // Prologue: S_A(0), S_B(0).
@@ -302,12 +305,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S_X(j+1) into the same TMEM columns (issued after, so executed after).
         for (int x = 0; x < 2; ++x) {
           if (j < nX[x]) {
+            if (!(ok = mbar_wait(&p_half[x], j & 1, abort_flag, p.status, 10 + x))) break;
+            tc_fence_after();
+            issue_pv(x, j, 0, BN / 32);
             if (!(ok = mbar_wait(&p_full[x], j & 1, abort_flag, p.status, 2 + 4 * x))) break;
             tc_fence_after();
 #ifdef SCREE_TRACE
             const long long t_is0 = clock64();
 #endif
-            issue_pv(x, j);
+            issue_pv(x, j, BN / 32, BN / 16);
+            umma_commit(&pv_done[x]);
             if (j + 1 < nX[x]) issue_s(x, j + 1);
 #ifdef SCREE_TRACE
             SCREE_TRACE_ADD(21, clock64() - t_is0);
@@ -394,22 +401,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_eff, -m_eff);
       uint64_t rs4[4] = {0ull, 0ull, 0ull, 0ull};  // (+0.0f, +0.0f) pairs
       uint32_t pk[BN / 2];
+      // Exponentiate and pack columns [c0, c1), two per packed f32x2 FMA / add;
+      // each pair of S values dies as its packed 16-bit word appears.
+      auto exp_pack = [&](int c0, int c1) {
 #pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        float x0, x1;
-        f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, negm2), x0, x1);
-        const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
-        const uint64_t e01 = f2_pack(e0, e1);
-        rs4[(c / 2) & 3] = f2_add(rs4[(c / 2) & 3], e01);
-        pk[c / 2] = Pk2<T>::pack(e0, e1);
-      }
-      float ra, rb;
-      f2_unpack(f2_add(f2_add(rs4[0], rs4[1]), f2_add(rs4[2], rs4[3])), ra, rb);
-      const float rs = ra + rb;
-#ifdef SCREE_TRACE
-      const long long t_ex = clock64();
-      SCREE_TRACE_ADD(24, t_ex - t_mx);
-#endif
+        for (int c = c0; c < c1; c += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, negm2), x0, x1);
+          const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
+          const uint64_t e01 = f2_pack(e0, e1);
+          rs4[(c / 2) & 3] = f2_add(rs4[(c / 2) & 3], e01);
+          pk[c / 2] = Pk2<T>::pack(e0, e1);
+        }
+      };
+      exp_pack(0, BN / 2);
       if (j >= 1) {
         // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
         // before P_X(j) overwrites the columns it read.  It already is in the
@@ -429,13 +434,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      l = l * alpha + rs;
-#ifdef SCREE_TRACE
-      const long long t_rs = clock64();
-      SCREE_TRACE_ADD(25, t_rs - t_ex);
-#endif
+      // First half of P_X(j): the MMA warp starts O_X += P V on it while the
+      // second half is formed.
       tmem_st32u(col_s, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_half[x]);
+      exp_pack(BN / 2, BN);
       tmem_st32u(col_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      float ra, rb;
+      f2_unpack(f2_add(f2_add(rs4[0], rs4[1]), f2_add(rs4[2], rs4[3])), ra, rb);
+      l = l * alpha + (ra + rb);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[x]);
