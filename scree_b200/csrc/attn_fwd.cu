@@ -50,6 +50,13 @@ constexpr int BN = 128;      // keys per K/V tile
 // 256 x 224 + 128 x 56 = 64,512 = 384 x 168.
 constexpr int kThreads = 384;
 constexpr int kRegsSoftmax = 224, kRegsOther = 56;
+// P_X(j) is handed to the MMA warp in kPParts parts (of BN / kPParts keys);
+// 2 parts measured 1.5% faster than 1 and 4% faster than 4 at cfg4.
+#ifndef SCREE_P_PARTS
+#define SCREE_P_PARTS 2
+#endif
+constexpr int kPParts = SCREE_P_PARTS;
+static_assert(kPParts == 2 || kPParts == 4, "P parts: 2 or 4");
 
 template <int D>
 struct FwdCfg {
@@ -67,7 +74,7 @@ struct FwdCfg {
   static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KSTAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + VSTAGES * KV_BYTES;
-  static constexpr int OFF_END = OFF_BAR + 192;
+  static constexpr int OFF_END = OFF_BAR + 256;  // mbarriers, TMEM slot, abort flag
   static constexpr int SMEM_RAW = OFF_END + 1024 <= 232448 ? OFF_END + 1024 : OFF_END;
   // At least 120 KB so that two CTAs (each holding all 512 TMEM columns) never
   // share an SM.
@@ -171,8 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* s_full = v_empty + C::VSTAGES;      // [2] per tile X
   uint64_t* p_full = s_full + 2;                // [2]
   uint64_t* pv_done = p_full + 2;               // [2]
-  uint64_t* p_half = pv_done + 2;               // [2] first half of P_X (keys 0..BN/2)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_half + 2);
+  uint64_t* p_part = pv_done + 2;               // [2][kPParts - 1] leading parts of P_X
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_part + 2 * (kPParts - 1));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -197,7 +204,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 128);
-      mbar_init(&p_half[x], 128);
+      for (int q = 0; q + 1 < kPParts; ++q) mbar_init(&p_part[x * (kPParts - 1) + q], 128);
       mbar_init(&pv_done[x], 1);
     }
     *abort_flag = 0;
@@ -305,15 +312,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S_X(j+1) into the same TMEM columns (issued after, so executed after).
         for (int x = 0; x < 2; ++x) {
           if (j < nX[x]) {
-            if (!(ok = mbar_wait(&p_half[x], j & 1, abort_flag, p.status, 10 + x))) break;
-            tc_fence_after();
-            issue_pv(x, j, 0, BN / 32);
+            constexpr int KK = BN / 16 / kPParts;  // PV k-steps per part of P
+            for (int q = 0; ok && q + 1 < kPParts; ++q) {
+              ok = mbar_wait(&p_part[x * (kPParts - 1) + q], j & 1, abort_flag, p.status, 10 + x);
+              tc_fence_after();
+              if (ok) issue_pv(x, j, q * KK, (q + 1) * KK);
+            }
+            if (!ok) break;
             if (!(ok = mbar_wait(&p_full[x], j & 1, abort_flag, p.status, 2 + 4 * x))) break;
             tc_fence_after();
 #ifdef SCREE_TRACE
             const long long t_is0 = clock64();
 #endif
-            issue_pv(x, j, BN / 32, BN / 16);
+            issue_pv(x, j, (kPParts - 1) * KK, BN / 16);
             umma_commit(&pv_done[x]);
             if (j + 1 < nX[x]) issue_s(x, j + 1);
 #ifdef SCREE_TRACE
@@ -414,7 +425,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[c / 2] = Pk2<T>::pack(e0, e1);
         }
       };
-      exp_pack(0, BN / 2);
+      constexpr int PC = BN / kPParts;  // keys per part of P
+      auto store_part = [&](int q) {   // packed columns [q PC / 2, (q + 1) PC / 2)
+        if constexpr (PC / 2 == 32)
+          tmem_st32u(col_s + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[q * 32]));
+        else
+          tmem_st16u(col_s + q * 16, &pk[q * 16]);
+      };
+      exp_pack(0, PC);
       if (j >= 1) {
         // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
         // before P_X(j) overwrites the columns it read.  It already is in the
@@ -434,14 +452,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // First half of P_X(j): the MMA warp starts O_X += P V on it while the
-      // second half is formed.
-      tmem_st32u(col_s, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_half[x]);
-      exp_pack(BN / 2, BN);
-      tmem_st32u(col_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      // P_X(j) is published part by part: the MMA warp starts O_X += P V on
+      // the first keys while the later ones are formed.
+#pragma unroll
+      for (int q = 0; q + 1 < kPParts; ++q) {
+        store_part(q);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_part[x * (kPParts - 1) + q]);
+        exp_pack((q + 1) * PC, (q + 2) * PC);
+      }
+      store_part(kPParts - 1);
       float ra, rb;
       f2_unpack(f2_add(f2_add(rs4[0], rs4[1]), f2_add(rs4[2], rs4[3])), ra, rb);
       l = l * alpha + (ra + rb);
