@@ -361,7 +361,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--config", default="cfg4", choices=["cfg4", "cfg2", "cfg5"])
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--non-causal", action="store_true")
@@ -513,30 +513,52 @@ def main():
         hq, hk, hv, hdo = (t.detach().cpu().pin_memory() for t in (q, k, v, do))
         ho = torch.empty_like(hq).pin_memory()
         hdq, hdk, hdv = (torch.empty_like(hq).pin_memory() for _ in range(3))
-        dq_ = torch.empty_like(q.detach())
+        # Pipelined steps: step i's host->device copies (copy-in stream) overlap
+        # step i-1's compute and step i-2's device->host copies (copy-out
+        # stream), as a serving or training loop feeding from pinned host
+        # memory would run.  Two device input sets; a set is rewritten only
+        # after the compute that read it has finished.
+        comp = torch.cuda.current_stream(dev)
+        cin = torch.cuda.Stream(dev)
+        cout = torch.cuda.Stream(dev)
+        bufs = [[torch.empty_like(q.detach()) for _ in range(4)] for _ in range(2)]
+        free_ev = [None, None]
 
-        def e2e_step():
-            dq_in = hq.to(dev, non_blocking=True).requires_grad_(True)
-            dk_in = hk.to(dev, non_blocking=True).requires_grad_(True)
-            dv_in = hv.to(dev, non_blocking=True).requires_grad_(True)
-            ddo = hdo.to(dev, non_blocking=True)
-            out = varlen_attention_triton_autograd(dq_in, dk_in, dv_in, cu, causal=causal)
-            out.backward(ddo)
-            ho.copy_(out.detach(), non_blocking=True)
-            hdq.copy_(dq_in.grad, non_blocking=True)
-            hdk.copy_(dk_in.grad, non_blocking=True)
-            hdv.copy_(dv_in.grad, non_blocking=True)
+        def e2e_step(i):
+            sset = bufs[i % 2]
+            with torch.cuda.stream(cin):
+                if free_ev[i % 2] is not None:
+                    cin.wait_event(free_ev[i % 2])
+                for b, hsrc in zip(sset, (hq, hk, hv, hdo)):
+                    b.copy_(hsrc, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(cin)
+            comp.wait_event(ready)
+            qi, ki, vi = (b.detach().requires_grad_(True) for b in sset[:3])
+            out = varlen_attention_triton_autograd(qi, ki, vi, cu, causal=causal)
+            out.backward(sset[3])
+            done = torch.cuda.Event()
+            done.record(comp)
+            free_ev[i % 2] = done
+            with torch.cuda.stream(cout):
+                cout.wait_event(done)
+                for hdst, t in zip((ho, hdq, hdk, hdv), (out.detach(), qi.grad, ki.grad, vi.grad)):
+                    hdst.copy_(t, non_blocking=True)
+                    t.record_stream(cout)
 
-        e2e_step()
+        e2e_step(0)
+        e2e_step(1)
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.e2e_steps):
-            e2e_step()
-        e1.record()
+        e0.record(comp)
+        cin.wait_stream(comp)  # the first copy starts inside the timed region
+        for i in range(args.e2e_steps):
+            e2e_step(i)
+        comp.wait_stream(cout)  # ... and the last copy back ends inside it
+        e1.record(comp)
         torch.cuda.synchronize()
         e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
         if world > 1:
@@ -549,9 +571,8 @@ def main():
             "ms_per_step": e_step,
             "h2d_bytes_per_step": int(4 * nbytes),  # q, k, v, dO
             "d2h_bytes_per_step": int(4 * nbytes),  # out, dq, dk, dv
-            "path": "varlen_attention_triton_autograd with pinned host q/k/v/dO in, out/dq/dk/dv back to pinned host",
+            "path": "varlen_attention_triton_autograd with pinned host q/k/v/dO in, out/dq/dk/dv back to pinned host; copies in, compute and copies out of consecutive steps overlap on three streams",
         }
-        del dq_
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
