@@ -249,7 +249,8 @@ def workload_config(args, lengths, H, D, causal, world):
         "heads": H,
         "head_dim": D,
         "causal": causal,
-        "parallelism": f"seq-shard{world}" if world > 1 else "single",
+        "parallelism": (f"{'head-group' if getattr(args, 'shard', 'seqs') == 'heads' else 'seq'}-shard{world}"
+                        if world > 1 else "single"),
         "l2": getattr(args, "l2_note", "inputs larger than L2"),
     }
 
@@ -365,6 +366,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--non-causal", action="store_true")
+    ap.add_argument("--shard", choices=["seqs", "heads"], default="seqs",
+                    help="multi-GPU split: whole sequences (default) or sequences split by head groups")
     ap.add_argument("--suite", choices=["attention", "norms"], default="attention",
                     help="norms: cfg3 RMSNorm/LayerNorm fwd+bwd and pack/unpack/to_padded/from_padded")
     ap.add_argument("--max-seqs", type=int, default=0, help="keep only the first N sequences (small profiling case)")
@@ -400,33 +403,51 @@ def main():
     from scree_b200 import _lib
     from scree_b200.kernels.native import varlen_attention_triton_autograd
 
-    # Shard plan: LPT on L^2 (attention cost), broadcast from rank 0.
+    # Shard plan, broadcast from rank 0: whole sequences by LPT on L^2, or
+    # (--shard heads) (sequence, head group) units; a rank runs one attention
+    # call per head count among its units.
     from scree_b200 import shard
 
-    plan = shard.plan_shards(lengths, world, cost="attention")
-    if world > 1:
-        plan = shard.broadcast_plan(plan)
-    mine = [lengths[i] for i in sorted(plan[rank])]
-    T = sum(mine)
+    if args.shard == "heads":
+        plan = shard.plan_units(lengths, world, H)
+        if world > 1:
+            plan = shard.broadcast_plan(plan)
+        groups = [(hs, [lengths[u.seq] for u in us])
+                  for hs, us in sorted(shard.units_by_heads(plan[rank]).items(), reverse=True)]
+        args.no_e2e = True  # the end-to-end path is measured on whole sequences
+    else:
+        plan = shard.plan_shards(lengths, world, cost="attention")
+        if world > 1:
+            plan = shard.broadcast_plan(plan)
+        groups = [(H, [lengths[i] for i in sorted(plan[rank])])]
+    # Tokens this rank covers: a sequence split over head groups counts its
+    # length times the fraction of heads each unit holds.
+    T = sum(sum(ls) * hs / H for hs, ls in groups)
     dt = getattr(torch, args.dtype_name)
     g = torch.Generator(device=dev).manual_seed(1234 + 17 * rank)
 
-    def rnd():
-        return torch.randn((T, H, D), device=dev, dtype=torch.float32, generator=g).to(dt)
+    calls = []  # (q, k, v, dO, cu) per head-count group
+    for hs, ls in groups:
+        Tg = sum(ls)
 
-    q, k, v, do = rnd(), rnd(), rnd(), rnd()
-    for t in (q, k, v):
-        t.requires_grad_(True)
-    cu = torch.tensor(np.concatenate([[0], np.cumsum(mine)]), dtype=torch.int32, device=dev)
+        def rnd():
+            return torch.randn((Tg, hs, D), device=dev, dtype=torch.float32, generator=g).to(dt)
+
+        qg, kg, vg, dog = rnd(), rnd(), rnd(), rnd()
+        for t in (qg, kg, vg):
+            t.requires_grad_(True)
+        cug = torch.tensor(np.concatenate([[0], np.cumsum(ls)]), dtype=torch.int32, device=dev)
+        calls.append((qg, kg, vg, dog, cug))
+    q, k, v, do, cu = calls[0]  # whole-sequence mode: the only group
 
     def step():
-        for t in (q, k, v):
-            t.grad = None
-        out = varlen_attention_triton_autograd(q, k, v, cu, causal=causal)
-        out.backward(do)
-        return out
+        for qg, kg, vg, dog, cug in calls:
+            for t in (qg, kg, vg):
+                t.grad = None
+            out = varlen_attention_triton_autograd(qg, kg, vg, cug, causal=causal)
+            out.backward(dog)
 
-    tensor_bytes = T * H * D * q.element_size()
+    tensor_bytes = sum(qg.numel() for qg, *_ in calls) * q.element_size()
     flush = None
     if tensor_bytes < L2_FLUSH_BYTES:
         flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
@@ -477,9 +498,9 @@ def main():
     sampler.stop()
     assert _lib.device_status() == 0, "kernel reported an error (device status word)"
 
-    flops_mine = workloads.attn_flops(mine, H, D, causal)
-    flops_fwd_mine = workloads.attn_flops(mine, H, D, causal, fwd=True, bwd=False)
-    flops_bwd_mine = workloads.attn_flops(mine, H, D, causal, fwd=False, bwd=True)
+    flops_mine = sum(workloads.attn_flops(ls, hs, D, causal) for hs, ls in groups)
+    flops_fwd_mine = sum(workloads.attn_flops(ls, hs, D, causal, fwd=True, bwd=False) for hs, ls in groups)
+    flops_bwd_mine = sum(workloads.attn_flops(ls, hs, D, causal, fwd=False, bwd=True) for hs, ls in groups)
     stats = torch.tensor([elapsed_ms, float(T), flops_mine, float(launches)], dtype=torch.float64, device=dev)
     if world > 1:
         mx = stats.clone()
@@ -497,8 +518,10 @@ def main():
     peak_tf = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
     bwd_avg_ms = bwd_ms / max(nb, 1)
     fwd_avg_ms = fwd_ms / max(nf, 1)
-    ach_bwd = flops_bwd_mine / (bwd_avg_ms / 1e3) / 1e12
-    ach_fwd = flops_fwd_mine / (fwd_avg_ms / 1e3) / 1e12
+    # This rank's FLOPs per step over its kernel time per step (one launch per
+    # step and kind, or one per head-count group with --shard heads).
+    ach_bwd = flops_bwd_mine / (bwd_ms / args.steps / 1e3) / 1e12
+    ach_fwd = flops_fwd_mine / (fwd_ms / args.steps / 1e3) / 1e12
     traffic = None
     tp = ROOT / "profiles" / "attn_bwd_cfg4_traffic.json"
     if tp.exists():

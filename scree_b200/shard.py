@@ -12,7 +12,12 @@ holds the host side of that:
   * LocalShard    a rank's sub-batch: its sequence indices, local offsets and
                   the global token rows they come from;
   * gather_to_rank0  per-rank outputs collected on rank 0 in global order
-                  (pad-to-max all_gather, since ranks hold different row counts).
+                  (pad-to-max all_gather, since ranks hold different row counts);
+  * plan_units    the same LPT over (sequence, head range) units: a sequence
+                  whose attention cost exceeds a fraction of a rank's share is
+                  split into equal head groups (each group's output rows are
+                  disjoint, so this stays reduction-free) -- batches dominated
+                  by one long sequence (cfg2, cfg5) balance this way.
 Multi-GPU runs use NCCL over NVLink for these collectives; the CPU tests use gloo.
 """
 
@@ -116,4 +121,55 @@ def gather_to_rank0(local_values, shard: LocalShard, total_rows: int, group=None
     for c, b, r in zip(counts, bufs, rbufs):
         if c:
             out[r[:c]] = b[:c]
+    return out
+
+
+@dataclass(frozen=True)
+class Unit:
+    """Attention work on heads [h0, h1) of one sequence."""
+
+    seq: int
+    h0: int
+    h1: int
+
+    @property
+    def heads(self) -> int:
+        return self.h1 - self.h0
+
+
+def plan_units(lengths: Sequence[int], world: int, heads: int, split_frac: float = 0.25,
+               max_groups: int = 16) -> List[List[Unit]]:
+    """Units per rank.  A sequence of cost L^2 * heads above split_frac times the
+    mean rank cost is cut into g equal head groups, g the smallest power of two
+    (at most max_groups, dividing heads) that brings each group under that
+    limit; units are then placed longest-first (LPT) on L^2 * (h1 - h0)."""
+    if world < 1 or heads < 1:
+        raise ValueError("world and heads must be >= 1")
+    total = sum(float(L) * float(L) * heads for L in lengths)
+    limit = split_frac * total / world
+    units: List[Unit] = []
+    for i, L in enumerate(lengths):
+        cost = float(L) * float(L) * heads
+        g = 1
+        while g < max_groups and heads % (2 * g) == 0 and cost / g > limit:
+            g *= 2
+        hs = heads // g
+        units.extend(Unit(i, k * hs, (k + 1) * hs) for k in range(g))
+    costs = [float(lengths[u.seq]) ** 2 * u.heads for u in units]
+    return [[units[j] for j in part] for part in lpt_partition(costs, world)]
+
+
+def units_imbalance(lengths: Sequence[int], plan: List[List[Unit]]) -> float:
+    """max rank cost / mean rank cost of a unit plan (1.0 = perfect)."""
+    loads = [sum(float(lengths[u.seq]) ** 2 * u.heads for u in part) for part in plan]
+    mean = sum(loads) / len(loads)
+    return max(loads) / mean if mean > 0 else 1.0
+
+
+def units_by_heads(plan_rank: List[Unit]):
+    """A rank's units grouped by head count: {heads: [Unit, ...]} in sequence
+    order; each group runs as one attention call over its sequences."""
+    out = {}
+    for u in sorted(plan_rank, key=lambda u: (u.seq, u.h0)):
+        out.setdefault(u.heads, []).append(u)
     return out
