@@ -138,11 +138,15 @@ class Unit:
 
 
 def plan_units(lengths: Sequence[int], world: int, heads: int, split_frac: float = 0.25,
-               max_groups: int = 16) -> List[List[Unit]]:
+               max_groups: int = 2) -> List[List[Unit]]:
     """Units per rank.  A sequence of cost L^2 * heads above split_frac times the
     mean rank cost is cut into g equal head groups, g the smallest power of two
     (at most max_groups, dividing heads) that brings each group under that
-    limit; units are then placed longest-first (LPT) on L^2 * (h1 - h0)."""
+    limit; units are then placed longest-first (LPT) on L^2 * (h1 - h0).
+    max_groups defaults to 2: every head group feeds a separate attention call
+    whose grid is tiles x heads, and measured on 4 B200s at cfg5, units of 1-2
+    heads left so few CTAs per call that the step took twice as long as with
+    whole sequences."""
     if world < 1 or heads < 1:
         raise ValueError("world and heads must be >= 1")
     total = sum(float(L) * float(L) * heads for L in lengths)

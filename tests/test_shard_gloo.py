@@ -108,7 +108,7 @@ def test_head_group_plan_covers_every_head_once_and_balances():
         cfg = workloads.attn_config(name)
         lengths, H = list(cfg.lengths), cfg.heads
         for world in (1, 2, 4, 8):
-            plan = shard.plan_units(lengths, world, H)
+            plan = shard.plan_units(lengths, world, H, max_groups=16)
             cover = np.zeros((len(lengths), H), dtype=np.int64)
             for part in plan:
                 for u in part:
@@ -118,7 +118,9 @@ def test_head_group_plan_covers_every_head_once_and_balances():
             assert shard.units_imbalance(lengths, plan) < 1.03, (name, world)
         if name in ("cfg2", "cfg5"):
             assert shard.imbalance(lengths, shard.plan_shards(lengths, 8)) > 1.9
-        groups = shard.units_by_heads(shard.plan_units(lengths, 8, H)[0])
+        # The default keeps every unit at half the heads or more.
+        assert all(u.heads >= H // 2 for part in shard.plan_units(lengths, 8, H) for u in part)
+        groups = shard.units_by_heads(shard.plan_units(lengths, 8, H, max_groups=16)[0])
         assert all(all(u.heads == hs for u in us) for hs, us in groups.items())
 
 
