@@ -874,10 +874,11 @@ BwdStreamPlan bwd_stream_plan(int64_t rows, int64_t C, int esize, bool aligned16
   if (!aligned16 || row_bytes % 16 != 0) return sp;
   const int64_t nv = row_bytes / 16;
   if (nv < 256 || nv > 4 * kBlock) return sp;
-  // 512 threads (one vector per thread per row) measured faster for RMSNorm at
-  // C = 4096; for LayerNorm (extra dbias partials, so 2 rows per block at 512
-  // threads) 256 threads measured faster.
-  sp.nt = (!layer && nv >= 2 * kBlock) ? 2 * kBlock : kBlock;
+  // 512 threads (one vector per thread per row) measured faster at C = 4096
+  // for both norms (LayerNorm 0.62 vs 0.58 of HBM, although its dbias partials
+  // spill a few registers at 512 threads x 4 rows); wider LayerNorm rows stay
+  // at 256 threads, where 4 vectors per thread would not fit.
+  sp.nt = (nv >= 2 * kBlock && (!layer || nv == 2 * kBlock)) ? 2 * kBlock : kBlock;
   sp.vpt = (int)((nv + sp.nt - 1) / sp.nt);
   if (sp.vpt == 3) sp.vpt = 4;
   sp.R = row_bytes <= 8192 ? 4 : (row_bytes <= 16384 ? 2 : 1);
@@ -915,11 +916,13 @@ int launch_bwd_stream(const BwdStreamPlan& sp, cudaStream_t s, const void* dy, c
   return launch_bwd_stream_r<T, WT, NTV, V, RR, LAYER>(sp, s, dy, x, w, mean, rstd, dx, pw, pb, \
                                                         rows, C)
   // The combinations stream_plan can produce (16-byte vectors per row nv,
-  // 256..1024): 256 threads with nv <= 256 / 512 / 1024, and for RMSNorm 512
-  // threads with nv = 512 / up to 1024; R follows from the row size.
+  // 256..1024): 256 threads with nv <= 256 / 512 / 1024, 512 threads with
+  // nv = 512, and for RMSNorm 512 threads with nv up to 1024; R follows from
+  // the row size.
   SCREE_BS(kBlock, 1, 4); SCREE_BS(kBlock, 2, 4); SCREE_BS(kBlock, 4, 2);
+  SCREE_BS(2 * kBlock, 1, 4);
   if constexpr (!LAYER) {
-    SCREE_BS(2 * kBlock, 1, 4); SCREE_BS(2 * kBlock, 2, 2);
+    SCREE_BS(2 * kBlock, 2, 2);
   }
 #undef SCREE_BS
   set_last_error("norm bwd: no streamed variant for nt=%d vpt=%d R=%d", sp.nt, sp.vpt, sp.R);
