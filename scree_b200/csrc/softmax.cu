@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kThreads, 4) softmax_bwd_kernel(const T* __res
 #pragma unroll
   for (int i = 0; i < VW; ++i) d[i] = 0.f;
   if (col_ok) {
-    constexpr int G = 2;
+    constexpr int G = 4;  // 4 rows of dy and y in flight per thread
     int64_t r = first;
     for (; r + (G - 1) * kRPC < r1; r += G * kRPC) {
       float g[G][VW], p[G][VW];
@@ -198,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 4) softmax_bwd_kernel(const T* __res
     d[i] = t;
   }
   if (!col_ok) return;
+#pragma unroll 2
   for (int64_t r = first; r < r1; r += kRPC) {
     float g[VW], p[VW];
     sload<T, VW>(dy + r * F + c0, g);
