@@ -198,8 +198,12 @@ __global__ void __launch_bounds__(kThreads, 4) softmax_bwd_kernel(const T* __res
     d[i] = t;
   }
   if (!col_ok) return;
+  // Pass 2 walks the rows backwards: the rows pass 1 read last are re-read
+  // first, while they are still in L2 (measured: 0.67 -> 0.68 of HBM; the
+  // forward, whose pass 2 reads one tensor, did not gain).
+  const int64_t last = first < r1 ? first + (r1 - 1 - first) / kRPC * kRPC : first - kRPC;
 #pragma unroll 2
-  for (int64_t r = first; r < r1; r += kRPC) {
+  for (int64_t r = last; r >= first; r -= kRPC) {
     float g[VW], p[VW];
     sload<T, VW>(dy + r * F + c0, g);
     sload<T, VW>(y + r * F + c0, p);
