@@ -36,13 +36,18 @@ typedef enum {
 
 typedef enum { SCREE_F16 = 0, SCREE_BF16 = 1, SCREE_F32 = 2 } scree_dtype;
 
+/* Codes of the device status word (scree_device_status). */
+#define SCREE_DEVERR_WAIT_TIMEOUT 1
+#define SCREE_DEVERR_BAD_INPUT 2
+
 /* Copies the calling thread's last error message into buf (NUL-terminated). */
 int scree_last_error(char* buf, size_t n);
 /* Returns SCREE_ABI_VERSION. */
 int scree_version(void);
 /* Reads (and optionally clears) the device status word that kernels set when a
- * bounded wait gave up or an input was out of range.  0 = no error.  This call
- * synchronises with the device. */
+ * bounded wait gave up or an input was out of range.  0 = no error, otherwise
+ * (code << 16) | site with code SCREE_DEVERR_WAIT_TIMEOUT (1) or
+ * SCREE_DEVERR_BAD_INPUT (2).  This call synchronises with the device. */
 int scree_device_status(int* status_out, int reset);
 /* Number of kernels this library has launched in the process so far. */
 long long scree_launch_count(void);
@@ -55,6 +60,28 @@ long long scree_launch_count(void);
 int scree_profile_enable(int on);
 int scree_profile_read(int kernel, double* total_ms, long long* launches);
 
+/* Device-side check of an offsets array (B+1 entries, int32 or int64):
+ * offsets[0] == 0, non-decreasing, offsets[B] == T.  Enqueued on `stream`; a
+ * violation sets the device status word to (SCREE_DEVERR_BAD_INPUT << 16) | 40,
+ * read with scree_device_status.  The attention entry points run the same check
+ * in their schedule kernel and then do no work at all on invalid offsets; the
+ * softmax and gather kernels skip (and report) any sequence whose range falls
+ * outside [0, T).  Replaces the invariant checks of scree/_core.py:44-62, which
+ * cover only offsets[0] and offsets[-1], with a full check on the device (no
+ * host synchronisation). */
+int scree_validate_offsets(const void* offsets, int offs_is_i64, int64_t B, int64_t T,
+                           void* stream);
+
+/* Self-test of failure detection (no reference counterpart): one GPU thread
+ * waits on an mbarrier that nothing arrives on, bounded by limit_ns (at most
+ * 1 s), exactly as every pipeline wait of the library is bounded.  When the
+ * limit expires the kernel writes 0 to *result_dev (device int; 1 if the wait
+ * had completed), sets the status word to (SCREE_DEVERR_WAIT_TIMEOUT << 16) | 99
+ * and returns, leaving the context usable.  Reset the status word before and
+ * after (scree_device_status with reset = 1): kernels skip their work while it
+ * holds an error. */
+int scree_selftest_wait_timeout(long long limit_ns, int* result_dev, void* stream);
+
 /* ------------------------------------------------------------------ attention
  * Varlen self-attention forward.
  * Replaces: scree/kernels/triton/varlen_attention.py:165-268
@@ -64,8 +91,10 @@ int scree_profile_read(int kernel, double* total_ms, long long* launches);
  * q, k, v, o: (T, H, D) fp16/bf16 with strides (row_stride, head_stride, 1)
  * in elements; o may alias nothing else.  lse: (T, H) fp32 contiguous, natural
  * log of the softmax denominator (m + ln l), or NULL.  scale is the softmax
- * scale (scree uses 1/sqrt(D)).  max_seqlen <= 0 means "unknown": the kernel
- * then sizes its grid for the worst case (T tokens in one sequence).
+ * scale (scree uses 1/sqrt(D)).  max_seqlen is accepted for signature
+ * compatibility and ignored: the work list is built on the device from the
+ * offsets, with no host synchronisation.  Invalid offsets (see
+ * scree_validate_offsets) make the call do no work and set the status word.
  * D must be 32, 64 or 128.  workspace: scree_attn_fwd_workspace_size() bytes. */
 size_t scree_attn_fwd_workspace_size(int64_t B, int64_t T, int64_t H, int D);
 int scree_attn_fwd(const void* q, const void* k, const void* v, int64_t q_row_stride,
@@ -85,7 +114,9 @@ int scree_attn_fwd(const void* q, const void* k, const void* v, int64_t q_row_st
  * batches return SCREE_ERR_INVALID.  All calls on a device share that array:
  * calls that overlap on the GPU race, so order them (one stream).  The first
  * call on a device resolves the array's address; make it before any stream
- * capture.  Allocates nothing. */
+ * capture.  That address is cached per device: after a cudaDeviceReset of a
+ * device, do not call this entry point on it again in the same process.
+ * Allocates nothing. */
 int scree_attn_fwd_noalloc(const void* q, const void* k, const void* v, int64_t q_row_stride,
                            int64_t q_head_stride, int64_t k_row_stride, int64_t k_head_stride,
                            int64_t v_row_stride, int64_t v_head_stride, const void* offsets,

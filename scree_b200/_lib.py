@@ -36,6 +36,8 @@ _SIGNATURES = {
     "scree_launch_count": (ctypes.c_longlong, []),
     "scree_profile_enable": (_I, [_I]),
     "scree_profile_read": (_I, [_I, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_longlong)]),
+    "scree_validate_offsets": (_I, [_P, _I, _L, _L, _P]),
+    "scree_selftest_wait_timeout": (_I, [ctypes.c_longlong, _P, _P]),
     "scree_attn_fwd_workspace_size": (_S, [_L, _L, _L, _I]),
     "scree_attn_fwd": (
         _I,
@@ -117,6 +119,38 @@ def device_status(reset: bool = True) -> int:
     v = ctypes.c_int(0)
     check(load().scree_device_status(ctypes.byref(v), 1 if reset else 0), "scree_device_status")
     return v.value
+
+
+DEVERR_WAIT_TIMEOUT = 1
+DEVERR_BAD_INPUT = 2
+_DEVERR_NAMES = {DEVERR_WAIT_TIMEOUT: "a bounded wait timed out", DEVERR_BAD_INPUT: "invalid input (offsets)"}
+
+
+def describe_status(status: int) -> str:
+    code, site = status >> 16, status & 0xFFFF
+    return f"{_DEVERR_NAMES.get(code, f'error code {code}')} at site {site}"
+
+
+def raise_device_status(reset: bool = True) -> None:
+    """Raise ScreeError if a kernel recorded an error in the device status word
+    (synchronises); clears the word when ``reset``."""
+    st = device_status(reset)
+    if st != 0:
+        raise ScreeError(f"libscree_b200 device status {st:#x}: {describe_status(st)}")
+
+
+def validate_offsets(offsets, total: int, stream=None) -> None:
+    """Enqueue the device-side offsets check (offsets[0] == 0, non-decreasing,
+    offsets[-1] == total); a violation shows up in the device status word."""
+    import torch
+
+    assert offsets.is_cuda and offsets.ndim == 1 and offsets.dtype in (torch.int32, torch.int64)
+    cu = offsets.contiguous()
+    s = stream if stream is not None else stream_ptr(cu.device)
+    with torch.cuda.device(cu.device):
+        rc = load().scree_validate_offsets(cu.data_ptr(), 1 if cu.dtype == torch.int64 else 0,
+                                           cu.numel() - 1, int(total), s)
+    check(rc, "scree_validate_offsets")
 
 
 PROF_ATTN_FWD, PROF_ATTN_BWD, PROF_NORM_FWD, PROF_NORM_BWD, PROF_GATHER = 0, 1, 2, 3, 4

@@ -127,6 +127,15 @@ template <> struct Pk2b<__half> {
   }
 };
 
+// TMEM column of k-step kk (16 queries) of a packed P^T / dS^T tile.  Each half
+// of the tile's queries is packed into the first half of its own fp32 columns:
+// queries [0, BQ/2) at columns [0, BQ/4), queries [BQ/2, BQ) at [BQ/2, 3BQ/4).
+template <int BQ>
+__device__ __forceinline__ uint32_t packed_col(int kk) {
+  constexpr int KH = BQ / 32;  // k-steps per half
+  return (uint32_t)((kk / KH) * (BQ / 2) + (kk % KH) * 8);
+}
+
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
                "f"(c), "f"(d)
@@ -320,8 +329,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + kk * 8, mnmaj<D>(ob, BQ, kk), ID_ACC,
-                      (it > 0 || kk > 0) ? 1u : 0u);  // A = P^T from TMEM (16 q = 8 columns)
+          umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + packed_col<BQ>(kk), mnmaj<D>(ob, BQ, kk),
+                      ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);  // A = P^T from TMEM
         umma_commit(p_free);
         // S^T for the next query tile overlaps the softmax warps' dS work.
         const bool more = it + 1 < n_it;
@@ -338,8 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk)
-          umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + kk * 8, mnmaj<D>(qb, BQ, kk), ID_ACC,
-                      (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + packed_col<BQ>(kk), mnmaj<D>(qb, BQ, kk),
+                      ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);
         if (more) issue_s_dp(it + 1, false);
         if (it > 0 && !(ok = mbar_wait(dq_empty, (it - 1) & 1, abort_flag, p.status, 27))) break;
         tc_fence_after();
@@ -424,8 +433,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = mbar_wait(p_free, (it - 1) & 1, abort_flag, p.status, 29);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       }
-      // P^T (16-bit, two per column): this half's QH/2 columns of S^T's first BQ/2.
-      tmem_st_packed<QH / 2>(lane_base + C::COL_S + hf * (QH / 2), pk);
+      // P^T (16-bit, two per column) over the first QH/2 of the QH fp32 columns
+      // this half read: never over the other half's columns (warps w and w+4
+      // share TMEM lanes and do not wait for each other).
+      tmem_st_packed<QH / 2>(lane_base + C::COL_S + hf * QH, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full);
@@ -455,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // dS^T: into TMEM over dP^T's first columns (A operand of dK) and into
       // smem (B operand of the dQ GEMM).
-      tmem_st_packed<QH / 2>(lane_base + C::COL_DP + hf * (QH / 2), pk);
+      tmem_st_packed<QH / 2>(lane_base + C::COL_DP + hf * QH, pk);
       write_row_sw128<T, QH>(smem + C::OFF_DS, kr, pr, hf * (QH / 8));
       tmem_wait_st();
       fence_proxy_async_smem();
@@ -681,7 +692,7 @@ int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v,
     else bwd_preprocess_kernel<T, 32><<<blocks, 256, 0, s>>>((const T*)o, (const T*)dout, lse, Tn, (int)H, deltaT, lse2T);
     SCREE_LAUNCH_CHECK();
   }
-  if ((rc = launch_build_schedule(offsets, is64, B, BN, (int)H, sched, s))) return rc;
+  if ((rc = launch_build_schedule(offsets, is64, B, Tn, BN, (int)H, sched, s))) return rc;
   BwdParams p;
   p.offs = offsets;
   p.is64 = is64;
@@ -740,7 +751,8 @@ extern "C" int scree_attn_bwd(const void* dout, const void* q, const void* k, co
     set_last_error("attn_bwd: head_dim %d unsupported (32, 64, 128)", D);
     return SCREE_ERR_UNSUPPORTED;
   }
-  SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16, "attn_bwd: fp16 or bf16 only");
+  SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16 || dtype == SCREE_F32,
+                  "attn_bwd: fp16, bf16 or fp32 only");
   if (T == 0) return SCREE_OK;
   SCREE_CHECK_ARG(dout && q && k && v && o && lse && offsets && dq && dk && dv,
                   "attn_bwd: null pointer");
@@ -753,6 +765,9 @@ extern "C" int scree_attn_bwd(const void* dout, const void* q, const void* k, co
   SCREE_BIND_DEVICE(stream, q);
   cudaStream_t s = (cudaStream_t)stream;
   char* ws = reinterpret_cast<char*>(workspace);
+  if (dtype == SCREE_F32)
+    return attn_bwd_f32(dout, q, k, v, o, lse, offsets, offs_is_i64, B, T, H, D, causal, scale, dq,
+                        dk, dv, reinterpret_cast<float*>(ws + L.off_delta), s);
   if (dtype == SCREE_BF16)
     return run_bwd_typed<__nv_bfloat16>(dout, q, k, v, o, lse, offsets, offs_is_i64, B, T, H, D,
                                         causal, scale, dq, dk, dv, ws, L, s);

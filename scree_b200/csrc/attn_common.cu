@@ -3,14 +3,41 @@
 
 namespace scree {
 
-// One CTA of 1024 threads.  Sorts (length, index) keys descending with a
-// shared-memory bitonic sort (B <= kSortMax), then an exclusive scan of
-// ntiles * H gives each sequence's first work item.
-__global__ void build_schedule_kernel(const void* offs, int is64, int64_t B, int outer, int H,
-                                      int64_t* total_out, SeqRef* refs) {
+// Whole-block check of an offsets array: offs[0] == 0, non-decreasing,
+// offs[B] == T.  Every thread of the block must call it (it ends in a barrier).
+__device__ bool offsets_valid_block(const void* offs, int is64, int64_t B, int64_t T) {
+  int bad = 0;
+  for (int64_t i = threadIdx.x; i < B; i += blockDim.x)
+    if (load_offset(offs, is64, i + 1) < load_offset(offs, is64, i)) bad = 1;
+  if (threadIdx.x == 0 && (load_offset(offs, is64, 0) != 0 || load_offset(offs, is64, B) != T))
+    bad = 1;
+  return __syncthreads_or(bad) == 0;
+}
+
+__global__ void validate_offsets_kernel(const void* offs, int is64, int64_t B, int64_t T,
+                                        int* status) {
+  if (!offsets_valid_block(offs, is64, B, T) && threadIdx.x == 0)
+    record_device_error(status, SCREE_DEVERR_BAD_INPUT, kSiteBadOffsets);
+}
+
+// One CTA of 1024 threads.  First validates the offsets (offs[0] == 0,
+// non-decreasing, offs[B] == T); invalid offsets record SCREE_DEVERR_BAD_INPUT
+// in the device status word and publish a schedule of zero items, so every
+// attention CTA exits before its first load or store.  Then sorts (length,
+// index) keys descending with a shared-memory bitonic sort (B <= kSortMax), and
+// an exclusive scan of ntiles * H gives each sequence's first work item.
+__global__ void build_schedule_kernel(const void* offs, int is64, int64_t B, int64_t T, int outer,
+                                      int H, int64_t* total_out, SeqRef* refs, int* status) {
   __shared__ unsigned long long keys[kSortMax];
   __shared__ long long warp_tot[32];
   __shared__ long long carry;
+  if (!offsets_valid_block(offs, is64, B, T)) {
+    if (threadIdx.x == 0) {
+      *total_out = 0;
+      record_device_error(status, SCREE_DEVERR_BAD_INPUT, kSiteBadOffsets);
+    }
+    return;
+  }
   const bool sorted = B <= kSortMax;
   int n2 = 1;
   while (n2 < B) n2 <<= 1;
@@ -80,14 +107,32 @@ __global__ void build_schedule_kernel(const void* offs, int is64, int64_t B, int
   if (threadIdx.x == 0) *total_out = carry;
 }
 
-int launch_build_schedule(const void* offs, int is64, int64_t B, int outer, int H, void* ws,
-                          cudaStream_t stream) {
-  build_schedule_kernel<<<1, 1024, 0, stream>>>(offs, is64, B, outer, H,
+int launch_build_schedule(const void* offs, int is64, int64_t B, int64_t T, int outer, int H,
+                          void* ws, cudaStream_t stream) {
+  build_schedule_kernel<<<1, 1024, 0, stream>>>(offs, is64, B, T, outer, H,
                                                 reinterpret_cast<int64_t*>(ws),
-                                                reinterpret_cast<SeqRef*>((char*)ws + 16));
+                                                reinterpret_cast<SeqRef*>((char*)ws + 16),
+                                                device_status_ptr());
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
+
+}  // namespace scree
+
+extern "C" int scree_validate_offsets(const void* offsets, int offs_is_i64, int64_t B, int64_t T,
+                                      void* stream) {
+  using namespace scree;
+  SCREE_CHECK_ARG(B >= 1 && T >= 0, "validate_offsets: bad sizes B=%lld T=%lld", (long long)B,
+                  (long long)T);
+  SCREE_CHECK_ARG(offsets != nullptr, "validate_offsets: null offsets");
+  SCREE_BIND_DEVICE(stream, offsets);
+  validate_offsets_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(offsets, offs_is_i64, B, T,
+                                                                 device_status_ptr());
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+namespace scree {
 
 EncodeTiledFn get_encode_tiled() {
   static EncodeTiledFn fn = nullptr;

@@ -32,8 +32,14 @@ inline size_t schedule_bytes(int64_t B) { return 16 + sizeof(SeqRef) * (size_t)B
 // larger batches keep their natural order (head-major grouping still applies).
 constexpr int kSortMax = 4096;
 
-int launch_build_schedule(const void* offs, int is64, int64_t B, int outer, int H, void* ws,
-                          cudaStream_t stream);
+// Status-word site of rejected offsets (attention schedule and softmax).
+constexpr int kSiteBadOffsets = 40;
+
+// Validates the offsets against T and builds the schedule into `ws`
+// (schedule_bytes(B)); invalid offsets give a zero-item schedule and a
+// SCREE_DEVERR_BAD_INPUT status.
+int launch_build_schedule(const void* offs, int is64, int64_t B, int64_t T, int outer, int H,
+                          void* ws, cudaStream_t stream);
 
 // Device side: item -> (seq, head, j) with j the rank of the tile within its
 // (seq, head) group (0 = first scheduled).
@@ -83,5 +89,15 @@ int make_thd_map(CUtensorMap* map, const void* base, int64_t T, int64_t H, int D
 // {D, 1, box_rows}, no swizzle; used as the target of TMA reduce-adds.
 int make_thd_map_f32(CUtensorMap* map, const void* base, int64_t T, int64_t H, int D,
                      int box_rows);
+
+// fp32 attention (attn_f32.cu): CUDA-core kernels for fp32 inputs.
+int attn_fwd_f32(const void* q, const void* k, const void* v, int64_t q_rs, int64_t q_hs,
+                 int64_t k_rs, int64_t k_hs, int64_t v_rs, int64_t v_hs, const void* offsets,
+                 int is64, int64_t B, int64_t T, int64_t H, int D, int causal, float scale,
+                 void* o, int64_t o_rs, int64_t o_hs, float* lse, cudaStream_t s);
+int attn_bwd_f32(const void* dout, const void* q, const void* k, const void* v, const void* o,
+                 const float* lse, const void* offsets, int is64, int64_t B, int64_t T, int64_t H,
+                 int D, int causal, float scale, void* dq, void* dk, void* dv, float* delta,
+                 cudaStream_t s);
 
 }  // namespace scree

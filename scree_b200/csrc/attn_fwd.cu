@@ -36,6 +36,7 @@ static __device__ unsigned long long g_fwd_trace[32];
   do { if ((threadIdx.x & 31) == 0 || (site) == 12) atomicAdd(&scree_trace_sm[(site) & 31], (unsigned long long)(cyc)); } while (0)
 static __shared__ unsigned long long scree_trace_sm[32];  // per-CTA, flushed at exit
 #endif
+#include <atomic>
 #include "attn_common.cuh"
 
 namespace scree {
@@ -565,9 +566,15 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
     set_last_error("attn_fwd: head_dim %d unsupported (32, 64, 128)", D);
     return SCREE_ERR_UNSUPPORTED;
   }
-  SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16, "attn_fwd: fp16 or bf16 only");
+  SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16 || dtype == SCREE_F32,
+                  "attn_fwd: fp16, bf16 or fp32 only");
   if (T == 0) return SCREE_OK;
   SCREE_CHECK_ARG(q && k && v && o && offsets, "attn_fwd: null pointer");
+  if (dtype == SCREE_F32) {  // CUDA-core fp32 kernels; no workspace needed
+    SCREE_BIND_DEVICE(stream, q);
+    return attn_fwd_f32(q, k, v, q_rs, q_hs, k_rs, k_hs, v_rs, v_hs, offsets, offs_is_i64, B, T,
+                        H, D, causal, scale, o, o_rs, o_hs, lse, (cudaStream_t)stream);
+  }
   SCREE_CHECK_ARG(workspace && workspace_bytes >= schedule_bytes(B),
                   "attn_fwd: workspace too small");
   SCREE_CHECK_ARG(((uintptr_t)o % 16) == 0 && (o_rs % 8) == 0 && (o_hs % 8) == 0,
@@ -581,7 +588,7 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
   if ((rc = make_thd_map(&tq, q, T, H, D, q_rs, q_hs, swb / 2, BM, swb, bf16))) return rc;
   if ((rc = make_thd_map(&tk, k, T, H, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
   if ((rc = make_thd_map(&tv, v, T, H, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
-  if ((rc = launch_build_schedule(offsets, offs_is_i64, B, ROWS, (int)H, workspace, s))) return rc;
+  if ((rc = launch_build_schedule(offsets, offs_is_i64, B, T, ROWS, (int)H, workspace, s))) return rc;
   FwdParams p;
   p.offs = offsets;
   p.is64 = offs_is_i64;
@@ -636,7 +643,9 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
 //    Serialise them, e.g. issue them on one stream.
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress, with that device current); make that first call
-//    before any stream capture.  Later calls reuse the cached address.
+//    before any stream capture.  Later calls reuse the cached address, which
+//    a cudaDeviceReset of that device makes stale: after a reset, do not call
+//    this entry point on that device again in the same process.
 // It allocates nothing itself: no cudaMalloc, cudaFree or allocating library
 // routine, and it then runs exactly the scree_attn_fwd path.
 namespace {
@@ -660,18 +669,20 @@ extern "C" int scree_attn_fwd_noalloc(const void* q, const void* k, const void* 
   // Make the device that owns the stream (or q) current, then resolve the
   // array's address on that device once.
   SCREE_BIND_DEVICE(stream, q);
-  static void* scratch_ptr[64] = {nullptr};
+  static std::atomic<void*> scratch_ptr[64];
   int dev = 0;
   SCREE_CUDA_TRY(cudaGetDevice(&dev));
   SCREE_CHECK_ARG(dev >= 0 && dev < 64, "attn_fwd_noalloc: device index %d out of range", dev);
-  if (scratch_ptr[dev] == nullptr) {
-    void* p = nullptr;
-    SCREE_CUDA_TRY(cudaGetSymbolAddress(&p, g_fwd_noalloc_scratch));
-    scratch_ptr[dev] = p;
+  void* scratch = scratch_ptr[dev].load(std::memory_order_acquire);
+  if (scratch == nullptr) {
+    // Concurrent first calls on one device resolve the same address; storing
+    // it twice is harmless.
+    SCREE_CUDA_TRY(cudaGetSymbolAddress(&scratch, g_fwd_noalloc_scratch));
+    scratch_ptr[dev].store(scratch, std::memory_order_release);
   }
   return scree_attn_fwd(q, k, v, q_rs, q_hs, k_rs, k_hs, v_rs, v_hs, offsets, offs_is_i64, B, T,
                         H, D, dtype, causal, scale, max_seqlen, o, o_rs, o_hs, lse,
-                        scratch_ptr[dev], kNoAllocScratchBytes, stream);
+                        scratch, kNoAllocScratchBytes, stream);
 }
 
 #ifdef SCREE_TRACE

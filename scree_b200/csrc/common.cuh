@@ -14,7 +14,7 @@ namespace scree {
 
 // Device status word: 0 = ok, otherwise (code << 16) | site of the first error.
 // It lives in common.cu; kernels receive its address (device_status_ptr()).
-enum : int { SCREE_DEVERR_WAIT_TIMEOUT = 1, SCREE_DEVERR_BAD_INPUT = 2 };
+// (codes SCREE_DEVERR_WAIT_TIMEOUT / SCREE_DEVERR_BAD_INPUT from scree_b200.h)
 
 __device__ __forceinline__ void record_device_error(int* status, int code, int site) {
   if (status) atomicCAS(status, 0, (code << 16) | (site & 0xFFFF));
@@ -79,12 +79,26 @@ int num_sms();  // cached SM count of the current device
 
 // Makes the device that owns `stream` (or, for the legacy default stream, the
 // memory `ptr` points to) current on the calling thread.  Callers such as
-// torch's autograd worker threads may enter with no CUDA context bound.
-int bind_device(cudaStream_t stream, const void* ptr);
-#define SCREE_BIND_DEVICE(stream, ptr)                          \
-  do {                                                          \
-    int _rc = ::scree::bind_device((cudaStream_t)(stream), ptr); \
-    if (_rc != SCREE_OK) return _rc;                            \
+// torch's autograd worker threads may enter with no CUDA context bound.  The
+// guard puts the caller's previous device back when the entry point returns,
+// if the caller had a context current (a thread with none is left bound to the
+// device it used, so no context is created on a device the process never used).
+struct DeviceGuard {
+  int prev = -1;
+  bool restore = false;
+  DeviceGuard() = default;
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+  ~DeviceGuard() {
+    if (restore) cudaSetDevice(prev);
+  }
+};
+int bind_device(cudaStream_t stream, const void* ptr, DeviceGuard* guard);
+#define SCREE_BIND_DEVICE(stream, ptr)                                                   \
+  ::scree::DeviceGuard _scree_device_guard;                                              \
+  do {                                                                                   \
+    int _rc = ::scree::bind_device((cudaStream_t)(stream), ptr, &_scree_device_guard);   \
+    if (_rc != SCREE_OK) return _rc;                                                     \
   } while (0)
 
 // Element <-> float conversion for the three activation dtypes.

@@ -36,13 +36,17 @@ template <> struct Vec<1> { using T = uint8_t; };
 // ---------------------------------------------------------------- pack
 template <int W>
 __global__ void __launch_bounds__(kThreads) pack_kernel(
-    const void* const* __restrict__ src, const void* offs, int is64, int64_t B,
-    int64_t row_bytes, int rows_per_cta, void* __restrict__ dst) {
+    const void* const* __restrict__ src, const void* offs, int is64, int64_t B, int64_t T,
+    int64_t row_bytes, int rows_per_cta, void* __restrict__ dst, int* status) {
   using V = typename Vec<W>::T;
   const uint32_t vpr = (uint32_t)(row_bytes / W);
   for (int64_t b = blockIdx.y; b < B; b += gridDim.y) {
     const int64_t s = load_offset(offs, is64, b);
     const int64_t len = load_offset(offs, is64, b + 1) - s;
+    if (s < 0 || len < 0 || s + len > T) {  // malformed offsets: no store, report
+      if (threadIdx.x == 0) record_device_error(status, SCREE_DEVERR_BAD_INPUT, 42);
+      continue;
+    }
     const int64_t j0 = (int64_t)blockIdx.x * rows_per_cta;
     if (j0 >= len) continue;
     const uint32_t nrows = (uint32_t)(rows_per_cta < len - j0 ? rows_per_cta : len - j0);
@@ -58,7 +62,7 @@ template <int W>
 __global__ void __launch_bounds__(kThreads) to_padded_kernel(
     const void* __restrict__ values, const void* offs, int is64, int64_t B, int64_t max_len,
     int64_t row_bytes, int rows_per_cta, uint4 fill16, int side_left, void* __restrict__ padded,
-    uint8_t* __restrict__ mask) {
+    uint8_t* __restrict__ mask, int* status) {
   using V = typename Vec<W>::T;
   V fill;
   memcpy(&fill, &fill16, sizeof(V));
@@ -66,6 +70,10 @@ __global__ void __launch_bounds__(kThreads) to_padded_kernel(
   for (int64_t b = blockIdx.y; b < B; b += gridDim.y) {
     const int64_t s = load_offset(offs, is64, b);
     const int64_t len = load_offset(offs, is64, b + 1) - s;
+    if (s < 0 || len < 0 || len > max_len) {  // malformed offsets: no access, report
+      if (threadIdx.x == 0) record_device_error(status, SCREE_DEVERR_BAD_INPUT, 43);
+      continue;
+    }
     const int64_t j0 = (int64_t)blockIdx.x * rows_per_cta;
     if (j0 >= max_len) continue;
     const uint32_t nrows = (uint32_t)(rows_per_cta < max_len - j0 ? rows_per_cta : max_len - j0);
@@ -200,7 +208,8 @@ extern "C" int scree_pack(const void* const* src_ptrs, const void* offsets, int 
   int rpc = 1;
   // CTAs past a sequence's end exit at once; without a bound, T rows.
   const dim3 grid = gather_grid(max_rows > 0 ? std::min(max_rows, T) : T, B, row_bytes, &rpc);
-  DISPATCH_WIDTH(w, pack_kernel, grid, s, src_ptrs, offsets, offs_is_i64, B, row_bytes, rpc, dst);
+  DISPATCH_WIDTH(w, pack_kernel, grid, s, src_ptrs, offsets, offs_is_i64, B, T, row_bytes, rpc, dst,
+                 device_status_ptr());
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
@@ -234,10 +243,11 @@ extern "C" int scree_to_padded(const void* values, const void* offsets, int offs
   // W-byte "vector" are walked over a null padded pointer with no stores.
   if (row_bytes == 0) {
     to_padded_kernel<1><<<grid, kThreads, 0, s>>>(values, offsets, offs_is_i64, B, max_len, 0,
-                                                   rpc, fill16, side_left, nullptr, mask);
+                                                   rpc, fill16, side_left, nullptr, mask,
+                                                   device_status_ptr());
   } else {
     DISPATCH_WIDTH(w, to_padded_kernel, grid, s, values, offsets, offs_is_i64, B, max_len,
-                   row_bytes, rpc, fill16, side_left, padded, mask);
+                   row_bytes, rpc, fill16, side_left, padded, mask, device_status_ptr());
   }
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;

@@ -64,7 +64,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait.  `abort` is a shared-memory flag: once any thread of the CTA gave
 // up, every later wait returns false immediately so all roles drain quickly.
 __device__ __forceinline__ bool mbar_wait_impl(uint64_t* bar, uint32_t parity,
-                                               volatile int* abort, int* status, int site) {
+                                               volatile int* abort, int* status, int site,
+                                               uint64_t limit_ns = SCREE_WAIT_LIMIT_NS) {
   if (mbar_try_wait(bar, parity)) return true;
   uint64_t t0 = global_timer_ns();
   uint32_t n = 0;
@@ -76,7 +77,7 @@ __device__ __forceinline__ bool mbar_wait_impl(uint64_t* bar, uint32_t parity,
         *abort = 1;  // another CTA already failed: drain
         return false;
       }
-      if (global_timer_ns() - t0 > SCREE_WAIT_LIMIT_NS) {
+      if (global_timer_ns() - t0 > limit_ns) {
         *abort = 1;
         record_device_error(status, SCREE_DEVERR_WAIT_TIMEOUT, site);
         return false;

@@ -47,13 +47,18 @@ constexpr float kLog2e = 1.4426950408889634f;
 template <typename T, int VW>
 __global__ void __launch_bounds__(kThreads, 4) softmax_fwd_kernel(const T* __restrict__ x,
                                                                 const void* offs, int is64,
-                                                                int64_t F, T* __restrict__ y) {
+                                                                int64_t T_, int64_t F,
+                                                                T* __restrict__ y, int* status) {
   __shared__ float sm_m[kRPC][kLPR * VW], sm_s[kRPC][kLPR * VW];
   __shared__ float fin_m[kLPR * VW], fin_s[kLPR * VW];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rsub = lane / kLPR, cv = lane % kLPR;
   const int64_t b = blockIdx.y;
   const int64_t r0 = load_offset(offs, is64, b), r1 = load_offset(offs, is64, b + 1);
+  if (r0 < 0 || r1 < r0 || r1 > T_) {  // malformed offsets: no access, report
+    if (threadIdx.x == 0) record_device_error(status, SCREE_DEVERR_BAD_INPUT, 41);
+    return;
+  }
   const int64_t c0 = (int64_t)blockIdx.x * kLPR * VW + cv * VW;
   const bool col_ok = c0 < F;  // F is a multiple of VW
   float m[VW], s[VW];
@@ -65,7 +70,7 @@ __global__ void __launch_bounds__(kThreads, 4) softmax_fwd_kernel(const T* __res
   const int64_t first = r0 + warp * kRPW + rsub;
   if (col_ok) {
     // Groups of G steps: one max update and one rescale per group, the group's
-    // loads issued together (G = 2 for 8-wide vectors keeps 64 registers).
+    // loads issued together (G = 4 rows of loads in flight per thread).
     constexpr int G = 4;
     int64_t r = first;
 #pragma unroll 1
@@ -148,12 +153,17 @@ template <typename T, int VW>
 __global__ void __launch_bounds__(kThreads, 4) softmax_bwd_kernel(const T* __restrict__ dy,
                                                                 const T* __restrict__ y,
                                                                 const void* offs, int is64,
-                                                                int64_t F, T* __restrict__ dx) {
+                                                                int64_t T_, int64_t F,
+                                                                T* __restrict__ dx, int* status) {
   __shared__ float sm_d[kWarps][kLPR * VW];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rsub = lane / kLPR, cv = lane % kLPR;
   const int64_t b = blockIdx.y;
   const int64_t r0 = load_offset(offs, is64, b), r1 = load_offset(offs, is64, b + 1);
+  if (r0 < 0 || r1 < r0 || r1 > T_) {  // malformed offsets: no access, report
+    if (threadIdx.x == 0) record_device_error(status, SCREE_DEVERR_BAD_INPUT, 41);
+    return;
+  }
   const int64_t c0 = (int64_t)blockIdx.x * kLPR * VW + cv * VW;
   const bool col_ok = c0 < F;
   const int64_t first = r0 + warp * kRPW + rsub;
@@ -215,7 +225,8 @@ __global__ void __launch_bounds__(kThreads, 4) softmax_bwd_kernel(const T* __res
 
 template <typename T>
 int launch(bool bwd, const void* a, const void* bb, const void* offs, int is64, int64_t B,
-           int64_t F, void* out, cudaStream_t s) {
+           int64_t Tn, int64_t F, void* out, cudaStream_t s) {
+  int* st = device_status_ptr();
   const bool vec = (F * (int64_t)sizeof(T)) % 16 == 0 && ((uintptr_t)a % 16) == 0 &&
                    ((uintptr_t)out % 16) == 0 && (!bwd || ((uintptr_t)bb % 16) == 0);
   constexpr int VWV = 16 / sizeof(T);
@@ -231,13 +242,13 @@ int launch(bool bwd, const void* a, const void* bb, const void* offs, int is64, 
                          : (const void*)((const int32_t*)offs + b0);
     const dim3 g(grid.x, (unsigned)nb, 1);
     if (!bwd) {
-      if (vec) softmax_fwd_kernel<T, VWV><<<g, kThreads, 0, s>>>((const T*)a, o, is64, F, (T*)out);
-      else softmax_fwd_kernel<T, 1><<<g, kThreads, 0, s>>>((const T*)a, o, is64, F, (T*)out);
+      if (vec) softmax_fwd_kernel<T, VWV><<<g, kThreads, 0, s>>>((const T*)a, o, is64, Tn, F, (T*)out, st);
+      else softmax_fwd_kernel<T, 1><<<g, kThreads, 0, s>>>((const T*)a, o, is64, Tn, F, (T*)out, st);
     } else {
       if (vec)
-        softmax_bwd_kernel<T, VWV><<<g, kThreads, 0, s>>>((const T*)a, (const T*)bb, o, is64, F, (T*)out);
+        softmax_bwd_kernel<T, VWV><<<g, kThreads, 0, s>>>((const T*)a, (const T*)bb, o, is64, Tn, F, (T*)out, st);
       else
-        softmax_bwd_kernel<T, 1><<<g, kThreads, 0, s>>>((const T*)a, (const T*)bb, o, is64, F, (T*)out);
+        softmax_bwd_kernel<T, 1><<<g, kThreads, 0, s>>>((const T*)a, (const T*)bb, o, is64, Tn, F, (T*)out, st);
     }
     SCREE_LAUNCH_CHECK();
   }
@@ -252,9 +263,9 @@ int dispatch(bool bwd, const void* a, const void* bb, const void* offs, int is64
   SCREE_BIND_DEVICE(stream, a);
   cudaStream_t s = (cudaStream_t)stream;
   switch (dtype) {
-    case SCREE_F16: return launch<__half>(bwd, a, bb, offs, is64, B, F, out, s);
-    case SCREE_BF16: return launch<__nv_bfloat16>(bwd, a, bb, offs, is64, B, F, out, s);
-    case SCREE_F32: return launch<float>(bwd, a, bb, offs, is64, B, F, out, s);
+    case SCREE_F16: return launch<__half>(bwd, a, bb, offs, is64, B, T, F, out, s);
+    case SCREE_BF16: return launch<__nv_bfloat16>(bwd, a, bb, offs, is64, B, T, F, out, s);
+    case SCREE_F32: return launch<float>(bwd, a, bb, offs, is64, B, T, F, out, s);
     default: break;
   }
   set_last_error("varlen softmax: unsupported dtype %d", dtype);

@@ -25,7 +25,10 @@ def _check_cuda(arr: Array, name: str) -> None:
 
 
 def varlen_attention(q: Array, k: Array, v: Array, causal: bool = False) -> Array:
-    """Varlen self-attention, scale 1/sqrt(head_dim); q, k, v (T, H, D) fp16/bf16."""
+    """Varlen self-attention, scale 1/sqrt(head_dim); q, k, v (T, H, D) with
+    head_dim 32, 64 or 128.  fp16 / bf16 run on the tcgen05 tensor-core kernels;
+    fp32 (the reference's Array-level default, reference/varlen_attention.py:90-114)
+    runs on fp32 CUDA-core kernels with fp32-grade results."""
     import torch
 
     for a in (q, k, v):
@@ -33,7 +36,10 @@ def varlen_attention(q: Array, k: Array, v: Array, causal: bool = False) -> Arra
     if not (q.offsets is k.offsets and q.offsets is v.offsets):
         if not (torch.equal(q.offsets, k.offsets) and torch.equal(q.offsets, v.offsets)):
             raise ValueError("q, k, v must have identical offsets")
-    out = native.varlen_attention_triton_autograd(q.values, k.values, v.values, q.offsets, causal=causal)
+    if q.values.dtype == torch.float32:
+        out = native.varlen_attention_fp32_autograd(q.values, k.values, v.values, q.offsets, causal=causal)
+    else:
+        out = native.varlen_attention_triton_autograd(q.values, k.values, v.values, q.offsets, causal=causal)
     return Array(values=out, offsets=q.offsets, ragged_dim=0, _host=q._host)
 
 

@@ -1,5 +1,16 @@
-"""Whether libscree_b200.so is present next to the package."""
+"""Whether libscree_b200.so is present next to the package and loads."""
 
-from .._lib import LIB_PATH
+from .._lib import load as _load
 
-NATIVE_AVAILABLE = LIB_PATH.exists()
+
+def _loads() -> bool:
+    try:
+        _load()
+    except OSError:
+        return False
+    except ImportError:
+        return False
+    return True
+
+
+NATIVE_AVAILABLE = _loads()

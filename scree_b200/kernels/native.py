@@ -34,6 +34,9 @@ __all__ = [
     "varlen_rmsnorm_autograd",
     "varlen_layernorm_autograd",
     "varlen_softmax_packed",
+    "varlen_attention_fp32",
+    "varlen_attention_fp32_backward",
+    "varlen_attention_fp32_autograd",
 ]
 
 
@@ -177,6 +180,78 @@ class _VarlenAttention(torch.autograd.Function):
 def varlen_attention_triton_autograd(q, k, v, cu_seqlens, causal: bool = False):
     """Autograd-aware varlen attention (scree/kernels/triton/_autograd.py:51)."""
     return _VarlenAttention.apply(q, k, v, cu_seqlens, causal)
+
+
+# --------------------------------------------------------------------------- fp32 attention
+
+
+def varlen_attention_fp32(q, k, v, cu_seqlens, causal: bool = False):
+    """fp32 varlen attention forward on CUDA-core fp32 kernels (fp32-grade
+    results); returns (out, lse).  The reference's Array-level op computes in the
+    caller's dtype, fp32 included (scree/kernels/reference/varlen_attention.py:90-114)."""
+    assert q.shape == k.shape == v.shape, "q, k, v must have identical shape"
+    assert q.is_cuda and q.dtype == torch.float32, "fp32 CUDA tensors expected"
+    assert k.dtype == q.dtype and v.dtype == q.dtype, "q, k, v must share a dtype"
+    total, n_heads, head_dim = q.shape
+    cu, is64 = _offsets_arg(cu_seqlens, q.device)
+    out = torch.empty_like(q, memory_format=torch.contiguous_format)
+    lse = torch.empty((total, n_heads), dtype=torch.float32, device=q.device)
+    if total == 0:
+        return out, lse
+    q, k, v = (t if t.stride(2) == 1 else t.contiguous() for t in (q, k, v))
+    with torch.cuda.device(q.device):
+        rc = _lib.load().scree_attn_fwd(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
+            cu.data_ptr(), is64, cu.numel() - 1, total, n_heads, head_dim, _lib.F32,
+            1 if causal else 0, 1.0 / math.sqrt(head_dim), 0,
+            out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), None, 0,
+            _lib.stream_ptr(q.device),
+        )
+    _lib.check(rc, "varlen_attention (fp32)")
+    return out, lse
+
+
+def varlen_attention_fp32_backward(do, q, k, v, o, lse, cu_seqlens, causal: bool = False):
+    """(dq, dk, dv) of varlen_attention_fp32, fp32 throughout, deterministic."""
+    total, n_heads, head_dim = q.shape
+    cu, is64 = _offsets_arg(cu_seqlens, q.device)
+    q, k, v, o, do = (t.contiguous() for t in (q, k, v, o, do))
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    if total == 0:
+        return dq, dk, dv
+    lib = _lib.load()
+    ws = torch.empty(lib.scree_attn_bwd_workspace_size(cu.numel() - 1, total, n_heads, head_dim),
+                     dtype=torch.uint8, device=q.device)
+    with torch.cuda.device(q.device):
+        rc = lib.scree_attn_bwd(
+            do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.contiguous().data_ptr(),
+            cu.data_ptr(), is64, cu.numel() - 1, total, n_heads, head_dim, _lib.F32,
+            1 if causal else 0, 1.0 / math.sqrt(head_dim), 0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+            ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device),
+        )
+    _lib.check(rc, "varlen_attention backward (fp32)")
+    return dq, dk, dv
+
+
+class _VarlenAttentionF32(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cu_seqlens, causal):
+        out, lse = varlen_attention_fp32(q, k, v, cu_seqlens, causal)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens)
+        ctx.causal = causal
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        q, k, v, out, lse, cu_seqlens = ctx.saved_tensors
+        dq, dk, dv = varlen_attention_fp32_backward(grad_output, q, k, v, out, lse, cu_seqlens, ctx.causal)
+        return dq, dk, dv, None, None
+
+
+def varlen_attention_fp32_autograd(q, k, v, cu_seqlens, causal: bool = False):
+    """Differentiable fp32 varlen attention (forward and backward on fp32 kernels)."""
+    return _VarlenAttentionF32.apply(q, k, v, cu_seqlens, causal)
 
 
 # --------------------------------------------------------------------------- norms

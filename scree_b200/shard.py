@@ -12,7 +12,7 @@ holds the host side of that:
   * LocalShard    a rank's sub-batch: its sequence indices, local offsets and
                   the global token rows they come from;
   * gather_to_rank0  per-rank outputs collected on rank 0 in global order
-                  (pad-to-max all_gather, since ranks hold different row counts);
+                  (point-to-point sends to rank 0 only);
   * plan_units    the same LPT over (sequence, head range) units: a sequence
                   whose attention cost exceeds a fraction of a rank's share is
                   split into equal head groups (each group's output rows are
@@ -53,12 +53,19 @@ def imbalance(lengths: Sequence[int], plan: List[List[int]], cost: str = "attent
 
 
 def broadcast_plan(plan: List[List[int]], group=None) -> List[List[int]]:
-    """Send rank 0's plan to every rank; raise if any rank had computed another."""
+    """Send rank 0's plan to every rank; if any rank had computed another, every
+    rank raises the same RuntimeError (an all-reduce MAX of a mismatch flag, so
+    no rank proceeds alone into the next collective)."""
+    import torch
     import torch.distributed as dist
 
     obj = [plan]
     dist.broadcast_object_list(obj, src=0, group=group)
-    if obj[0] != plan:
+    backend = dist.get_backend(group)
+    dev = torch.device("cuda", torch.cuda.current_device()) if backend == "nccl" else torch.device("cpu")
+    flag = torch.tensor([0 if obj[0] == plan else 1], dtype=torch.int32, device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+    if int(flag.item()) != 0:
         raise RuntimeError("shard plan differs across ranks (inputs or seeds disagree)")
     return obj[0]
 
@@ -91,36 +98,68 @@ def local_shard(global_offsets: Sequence[int], plan: List[List[int]], rank: int)
     return LocalShard(seqs, lengths, offs, rows)
 
 
-def gather_to_rank0(local_values, shard: LocalShard, total_rows: int, group=None):
+def gather_to_rank0(local_values, shard: LocalShard, total_rows: int, group=None,
+                    plan: List[List[int]] | None = None, global_offsets=None):
     """All ranks pass their (T_r, ...) values; rank 0 receives the (T, ...) tensor
-    in global row order, other ranks receive None.  Pads to the largest T_r and
-    uses all_gather (NCCL on GPUs, gloo on CPU)."""
+    in global row order, other ranks receive None.
+
+    Point-to-point: every rank r > 0 sends its rows to rank 0 (NCCL send/recv
+    over NVLink on GPUs, gloo on CPU); no rank but 0 receives anything.  When
+    ``plan`` and ``global_offsets`` are given, every rank derives all ranks'
+    row lists from them and nothing but the values crosses the wire; otherwise
+    the row counts and row indices are sent first."""
     import torch
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     dev = local_values.device
-    n = torch.tensor([local_values.shape[0]], dtype=torch.int64, device=dev)
-    ns = [torch.zeros_like(n) for _ in range(world)]
-    dist.all_gather(ns, n, group=group)
-    counts = [int(c.item()) for c in ns]
-    tmax = max(counts) if counts else 0
     feat = tuple(local_values.shape[1:])
-    padded = torch.zeros((tmax, *feat), dtype=local_values.dtype, device=dev)
-    padded[: local_values.shape[0]] = local_values
-    rows = torch.full((tmax,), -1, dtype=torch.int64, device=dev)
-    rows[: shard.rows.shape[0]] = torch.as_tensor(shard.rows, device=dev)
-    bufs = [torch.empty_like(padded) for _ in range(world)]
-    rbufs = [torch.empty_like(rows) for _ in range(world)]
-    dist.all_gather(bufs, padded, group=group)
-    dist.all_gather(rbufs, rows, group=group)
+    vals = local_values.contiguous()
+    if plan is not None and global_offsets is not None:
+        rows_of = [torch.as_tensor(local_shard(global_offsets, plan, r).rows, device=dev)
+                   for r in range(world)]
+        counts = [int(r_.shape[0]) for r_ in rows_of]
+    else:
+        n = torch.tensor([vals.shape[0]], dtype=torch.int64, device=dev)
+        ns = [torch.zeros_like(n) for _ in range(world)] if rank == 0 else None
+        dist.gather(n, ns, dst=0, group=group)
+        counts = [int(c.item()) for c in ns] if rank == 0 else None
+        rows_of = None
+    g0 = dist.get_global_rank(group, 0) if group is not None else 0
+
+    def gr(r):
+        return dist.get_global_rank(group, r) if group is not None else r
+
     if rank != 0:
+        ops = []
+        if vals.shape[0]:
+            ops.append(dist.P2POp(dist.isend, vals, g0, group))
+        if rows_of is None:
+            my_rows = torch.as_tensor(shard.rows, dtype=torch.int64, device=dev)
+            if my_rows.shape[0]:
+                ops.append(dist.P2POp(dist.isend, my_rows, g0, group))
+        for w in dist.batch_isend_irecv(ops) if ops else []:
+            w.wait()
         return None
-    out = torch.empty((total_rows, *feat), dtype=local_values.dtype, device=dev)
-    for c, b, r in zip(counts, bufs, rbufs):
-        if c:
-            out[r[:c]] = b[:c]
+    bufs, rbufs, ops = {}, {}, []
+    for r in range(1, world):
+        if counts[r] == 0:
+            continue
+        bufs[r] = torch.empty((counts[r], *feat), dtype=vals.dtype, device=dev)
+        ops.append(dist.P2POp(dist.irecv, bufs[r], gr(r), group))
+        if rows_of is None:
+            rbufs[r] = torch.empty((counts[r],), dtype=torch.int64, device=dev)
+            ops.append(dist.P2POp(dist.irecv, rbufs[r], gr(r), group))
+    for w in dist.batch_isend_irecv(ops) if ops else []:
+        w.wait()
+    out = torch.empty((total_rows, *feat), dtype=vals.dtype, device=dev)
+    mine = rows_of[0] if rows_of is not None else torch.as_tensor(shard.rows, dtype=torch.int64, device=dev)
+    if mine.shape[0]:
+        out.index_copy_(0, mine, vals)
+    for r, b in bufs.items():
+        idx = rows_of[r] if rows_of is not None else rbufs[r]
+        out.index_copy_(0, idx, b)
     return out
 
 

@@ -44,7 +44,7 @@ def test_argument_validation_without_gpu():
     with pytest.raises(ValueError):
         _lib.check(rc, "attn")
     rc = lib.scree_attn_bwd(None, None, None, None, None, None, None, 0, 1, 10, 1, 64, 2, 0, 1.0, 0, None, None, None, None, 0, None)
-    assert rc == _lib.SCREE_ERR_INVALID  # fp32 attention is rejected
+    assert rc == _lib.SCREE_ERR_INVALID  # null pointers are rejected before any CUDA call
     assert lib.scree_pack(None, None, 0, 0, 0, 0, 0, 16, None, None) == _lib.SCREE_ERR_INVALID
     assert lib.scree_to_padded(None, None, 0, 1, 1, 4, 3, None, 0, None, None, None) == _lib.SCREE_ERR_INVALID
 

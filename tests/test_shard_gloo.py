@@ -55,7 +55,10 @@ def _worker(rank, world, port, mode, q):
             except Exception as e:  # the missing rank must surface as an error
                 q.put((rank, "error", type(e).__name__))
             return
-        out = shard.gather_to_rank0(vals, mine, int(offs[-1]))
+        if mode == "ok_plan":  # row lists derived from the plan: only values are sent
+            out = shard.gather_to_rank0(vals, mine, int(offs[-1]), plan=plan, global_offsets=offs)
+        else:
+            out = shard.gather_to_rank0(vals, mine, int(offs[-1]))
         if rank == 0:
             ok = torch.equal(out[:, 0], torch.arange(int(offs[-1]), dtype=torch.float64) * 2.0)
             q.put((rank, "gathered", ok))
@@ -130,9 +133,20 @@ def test_two_ranks_gather_global_order():
     assert res[0][2] is True and res[1][2] is True
 
 
+@pytest.mark.parametrize("mode", ["ok", "ok_plan"])
+def test_three_ranks_gather_point_to_point(mode):
+    """Ranks 1 and 2 send to rank 0 only; rank 0 rebuilds global order, with the
+    row lists sent or derived from the plan."""
+    res = _run(mode, world=3)
+    assert [r[1] for r in res] == ["gathered", "sent", "sent"], res
+    assert all(r[2] is True for r in res), res
+
+
 def test_two_ranks_detect_plan_disagreement():
+    """Both ranks, rank 0 included (its own plan matches itself), raise the
+    same mismatch error instead of one rank proceeding into the next collective."""
     res = _run("disagree")
-    assert any(r[1] == "plan-mismatch" for r in res), res
+    assert len(res) == 2 and all(r[1] == "plan-mismatch" for r in res), res
 
 
 def test_missing_rank_is_an_error_not_a_hang():
