@@ -7,23 +7,30 @@ Workload (default): cfg4 — 64 sequences, lengths lognormal(ln 2048, 0.6) clipp
 to [16, 16384] at seed 0 (T = 158,330 tokens), q/k/v/dO ~ N(0,1) bf16 of shape
 (T, 32 heads, 128), causal.  A step is one forward + backward through the
 drop-in autograd entry point (varlen_attention_triton_autograd -> out.backward).
-At cfg4 every q/k/v/dO tensor is 1.3 GB, far larger than the 126 MB L2, so no
-flush is needed between steps; when a rank's tensors are under 256 MB (cfg2,
-cfg5, cfg4 split 8 ways) a 256 MB buffer is written before every timed step,
-outside that step's CUDA events.
+
+Timing, identical at every N: each timed step has its own CUDA-event pair on
+the compute stream, and a 256 MB buffer (twice the 126 MB L2) is written
+before every step, outside its events; the step times are summed.
 
 Multi-GPU (torchrun, one process per GPU): the fixed batch is split by whole
 sequences, longest-processing-time-first on L^2, identically on every rank (the
-plan is broadcast from rank 0 over NCCL as a consistency check).  There is no
-collective on the data path; the step time is the max over ranks (CUDA events,
-all_reduce MAX) and ``value`` = all tokens / that time ("strong" scaling: total
-work fixed).
+plan is broadcast from rank 0 over NCCL and checked).  ``value`` is the
+compute-only throughput (every rank keeps its outputs, as a data-parallel rank
+does): all tokens / the max over ranks of the step time ("strong" scaling:
+total work fixed).  ``with_gather`` adds the exchange of the per-rank outputs
+(O, dQ, dK, dV) to rank 0 by NCCL send/recv inside every step and reports that
+time too.
+
+At N=1 the same line also carries ``norms``: cfg3 RMSNorm / LayerNorm forward
+and backward, varlen softmax and the pack / to_padded / from_padded gathers,
+each timed per launch with CUDA events (L2 flushed before each), as GB/s of
+algorithmic bytes and as a fraction of the measured HBM bandwidth.
 
 --impl reference times the reference algorithm on the host CPU instead: the
 numpy oracle (a restatement of scree.kernels.reference; the reference itself is
-pure Python and is not installed on the GPU box), fp32, all host cores, on a
-bounded sample of cfg4's sequences, extrapolated to the whole workload by
-algorithmic FLOPs.
+pure Python and is not installed on the GPU box), fp32, all host threads.  Each
+step processes one of the 32 heads of every cfg4 sequence (heads are
+independent and cost the same); the value is scaled by the head count.
 """
 
 from __future__ import annotations
@@ -46,6 +53,35 @@ sys.path.insert(0, str(ROOT))
 METRIC = "varlen-attn fwd+bwd tokens/s & TFLOP/s vs TC peak at 1/2/4/8 B200"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 * 1024 * 1024  # 2x the 126 MB L2
+CLOCK_PERIOD_S = 0.05
+
+
+TRAFFIC_FILE = ROOT / "profiles" / "attn_bwd_small_traffic.json"
+
+
+def scaled_traffic(groups, D, causal):
+    """DRAM bytes per backward launch for this rank's workload, scaled from one
+    ncu capture of dram__bytes_read.sum + dram__bytes_write.sum on a small case
+    (TRAFFIC_FILE) by the ratio of causal pairs x heads (the backward's traffic
+    grows with the (key tile, query tile) pairs: Q/dO re-reads and the fp32 dQ
+    accumulation).  Returns (bytes or None, description)."""
+    from scree_b200 import workloads
+
+    if not TRAFFIC_FILE.exists():
+        return None, "no capture"
+    try:
+        d = json.loads(TRAFFIC_FILE.read_text())
+        units_small = float(d["pairs_x_heads"])
+        units = float(sum((workloads.causal_pairs(ls) if causal else sum(L * L for L in ls)) * hs
+                          for hs, ls in groups))
+        if d.get("head_dim") != D:
+            return None, "capture has another head_dim"
+        scale = units / units_small
+        return float(d["bytes_per_launch"]) * scale, (
+            f"{d['bytes_per_launch'] / 1e9:.3f} GB per launch measured by ncu on {d['case']} "
+            f"({TRAFFIC_FILE.name}), scaled x{scale:.2f} by causal pairs x heads")
+    except Exception as e:  # malformed file: report, do not guess
+        return None, f"unreadable capture: {e}"
 
 
 def load_peaks():
@@ -71,7 +107,7 @@ _REASONS = {
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons every 200 ms through NVML (read only)."""
+    """Samples SM clock and clock-event reasons every 50 ms through NVML (read only)."""
 
     def __init__(self, device_index: int):
         self.samples = []
@@ -108,7 +144,7 @@ class ClockSampler:
                 self.samples.append((mhz, rs))
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(CLOCK_PERIOD_S)
 
     def start(self):
         if self.ok:
@@ -137,43 +173,46 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU arm
-def cpu_reference_rate(lengths, H, D, causal, budget_s=12.0, repeats=2, log=None):
-    """Time the oracle (numpy fp32, all host cores) forward+backward on a bounded
-    sample of the workload's sequences and extrapolate to the whole workload by
-    algorithmic FLOPs.  Returns (tokens/s, cores, sample description)."""
-    import oracle
-    from scree_b200 import workloads
-
+def _cpu_threads():
+    """Host threads for the numpy oracle, with BLAS / OpenMP pools raised to
+    all of them (torchrun sets OMP_NUM_THREADS=1 for its ranks)."""
     cores = len(os.sched_getaffinity(0))
-    T_total = sum(lengths)
-    F_total = workloads.attn_flops(lengths, H, D, causal)
-    # Sample: the median-length sequence, all heads (cost per token of the batch
-    # is dominated by pair count, which the FLOP scaling accounts for).
-    order = np.argsort(lengths)
-    L = int(lengths[int(order[len(order) // 2])])
-    rng = np.random.default_rng(0)
-    q, k, v, do = (rng.standard_normal((L, H, D)).astype(np.float32) for _ in range(4))
-    offs = [0, L]
+    try:
+        import threadpoolctl
 
-    def run():
-        oracle.attention_fwd(q, k, v, offs, causal=causal, dtype=np.float32)
-        oracle.attention_bwd(do, q, k, v, offs, causal=causal, dtype=np.float32)
+        threadpoolctl.threadpool_limits(cores)
+    except Exception:
+        pass
+    return cores
 
-    run()  # warm-up
-    times = []
-    t_start = time.perf_counter()
-    for _ in range(repeats):
-        t0 = time.perf_counter()
-        run()
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() - t_start > budget_s:
-            break
+
+def _cpu_head_step(lengths, H, D, causal, head, seed=0):
+    """One step of the CPU sample: the numpy oracle's fwd+bwd (fp32) on head
+    `head` of every sequence of the workload.  Inputs are drawn per head from a
+    seeded generator (N(0,1), as on the GPU)."""
+    import oracle
+
+    rng = np.random.default_rng(seed + head)
+    offs = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    T = int(offs[-1])
+    q, k, v, do = (rng.standard_normal((T, 1, D), dtype=np.float32) for _ in range(4))
+    t0 = time.perf_counter()
+    oracle.attention_fwd(q, k, v, offs, causal=causal, dtype=np.float32)
+    oracle.attention_bwd(do, q, k, v, offs, causal=causal, dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def cpu_reference_rate(lengths, H, D, causal, repeats=2):
+    """CPU baseline for the GPU line: the oracle on one head of every sequence,
+    `repeats` times (about 10-20 s); tokens/s = T / (H x median head time)."""
+    cores = _cpu_threads()
+    times = [_cpu_head_step(lengths, H, D, causal, head=h) for h in range(repeats)]
     t = statistics.median(times)
-    F_sample = workloads.attn_flops([L], H, D, causal)
-    rate = T_total / (t * F_total / F_sample)
-    sample = (f"one sequence of L={L} (cfg4 median) x {H} heads x D={D}, fp32 numpy oracle "
-              f"fwd+bwd, median of {len(times)} after 1 warm-up = {t:.3f} s; extrapolated to "
-              f"all {len(lengths)} sequences by algorithmic FLOPs ({F_total / F_sample:.1f}x)")
+    T = sum(lengths)
+    rate = T / (t * H)
+    sample = (f"numpy oracle (restatement of scree.kernels.reference) fp32 fwd+bwd of 1 of {H} heads "
+              f"over all {len(lengths)} sequences (T={T}, D={D}), median of {len(times)} heads = {t:.2f} s; "
+              f"x{H} heads (independent, identical cost) for the whole workload")
     return rate, cores, sample
 
 
@@ -182,34 +221,17 @@ def run_reference_arm(args, lengths, H, D, causal):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    import oracle
-    from scree_b200 import workloads
-
-    cores = len(os.sched_getaffinity(0))
-    order = np.argsort(lengths)
-    L = int(lengths[int(order[len(order) // 2])])
-    rng = np.random.default_rng(0)
-    q, k, v, do = (rng.standard_normal((L, H, D)).astype(np.float32) for _ in range(4))
-    offs = [0, L]
-
-    def step():
-        oracle.attention_fwd(q, k, v, offs, causal=causal, dtype=np.float32)
-        oracle.attention_bwd(do, q, k, v, offs, causal=causal, dtype=np.float32)
-
-    for _ in range(args.warmup):
-        step()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        step()
-    dt = (time.perf_counter() - t0) / args.steps
+    cores = _cpu_threads()
+    for i in range(args.warmup):
+        _cpu_head_step(lengths, H, D, causal, head=i % H)
+    times = [_cpu_head_step(lengths, H, D, causal, head=i % H) for i in range(args.steps)]
+    dt = sum(times) / len(times)
     T_total = sum(lengths)
-    F_total = workloads.attn_flops(lengths, H, D, causal)
-    F_sample = workloads.attn_flops([L], H, D, causal)
-    step_full = dt * F_total / F_sample
-    value = T_total / step_full
-    sample = (f"each step: one sequence of L={L} (cfg4 median) x {H} heads x D={D}, numpy oracle "
-              f"(restatement of scree.kernels.reference) fp32 fwd+bwd on {cores} host threads, "
-              f"extrapolated to the whole workload by algorithmic FLOPs ({F_total / F_sample:.1f}x)")
+    value = T_total / (dt * H)
+    sample = (f"each step: numpy oracle (restatement of scree.kernels.reference) fp32 fwd+bwd of one of "
+              f"the {H} heads (rotating) over all {len(lengths)} sequences (T={T_total}, D={D}) on {cores} "
+              f"host threads, {dt:.2f} s per head; value = T / ({H} x that time): heads are independent "
+              f"and cost the same")
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -218,18 +240,25 @@ def run_reference_arm(args, lengths, H, D, causal):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": step_full * 1e3,
+        "ms_per_step": dt * 1e3,
+        "ms_per_step_note": "time of one step of the sample (one head of every sequence)",
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic",
         "config": workload_config(args, lengths, H, D, causal, world),
-        "tflops": F_total / step_full / 1e12,
+        "tflops": workloads_flops(lengths, 1, D, causal) / dt / 1e12,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def workloads_flops(lengths, H, D, causal):
+    from scree_b200 import workloads
+
+    return workloads.attn_flops(lengths, H, D, causal)
 
 
 _LEN_DESC = {
@@ -256,19 +285,19 @@ def workload_config(args, lengths, H, D, causal, world):
 
 
 # ----------------------------------------------------------------------------- norms suite
-def run_norm_suite(args):
+def measure_norms(steps, warmup, with_cpu=True):
     """cfg3: 64 sequences, lengths lognormal(ln 256, 0.6) (T = 19,794), hidden 4096
     bf16.  Each op is timed per launch with CUDA events; a 256 MB buffer is
     written between launches to flush the 126 MB L2.  Bandwidth = algorithmic
-    bytes (reads + writes the op must do) / time, against MEASURED_PEAKS hbm_gbs."""
+    bytes (reads + writes the op must do) / time, against MEASURED_PEAKS hbm_gbs.
+    Returns (per-op results, cpu baseline or None, hbm peak, peak source, T)."""
     import torch
 
     import scree_b200 as scree
     from scree_b200 import _lib, workloads
     from scree_b200.kernels import native
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    dev = torch.device("cuda", torch.cuda.current_device())
     lengths = workloads.cfg3_lengths()
     T, C, b = sum(lengths), 4096, 2
     g = torch.Generator(device=dev).manual_seed(0)
@@ -283,7 +312,7 @@ def run_norm_suite(args):
     padded, mask = scree.to_padded(arr)
     _, rstd = native._rmsnorm_fwd(x, w, 1e-5, True)
     _, mean, rstd_l = native._layernorm_fwd(x, w, bias, 1e-5, True)
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     sm_y = native.varlen_softmax_packed(x, offs)
     sm_dx = torch.empty_like(x)
     B = len(lengths)
@@ -302,38 +331,48 @@ def run_norm_suite(args):
     hbm = float(peaks["hbm_gbs"])
     res = {}
     for name, (fn, nbytes) in ops.items():
-        for _ in range(max(3, args.warmup)):
+        for _ in range(max(3, warmup)):
             fn()
         # Kernel-only time from the library's CUDA-event hooks around each
-        # launch; the 256 MB flush is written before every launch.
-        # (the softmax kernels report under the norm fwd / bwd event kinds)
+        # launch (all launches of one call summed); the 256 MB flush is written
+        # before every call.  The softmax kernels report under the norm fwd /
+        # bwd event kinds.
         kind_ = _lib.PROF_NORM_FWD if name.endswith("_fwd") else (_lib.PROF_NORM_BWD if name.endswith("_bwd") else _lib.PROF_GATHER)
         times = []
         _lib.profile_read(kind_)
         _lib.profile_enable(True)
-        for _ in range(args.steps):
+        for _ in range(steps):
             flush.fill_(1)
             fn()
             torch.cuda.synchronize()
-            tms, nl = _lib.profile_read(kind_)
-            times.append(tms / max(nl, 1) * max(nl, 1))  # all launches of one call
+            tms, _nl = _lib.profile_read(kind_)
+            times.append(tms)
         _lib.profile_enable(False)
         ms = statistics.median(times)
         gbs = nbytes / (ms / 1e3) / 1e9
         res[name] = {"ms": ms, "algorithmic_bytes": int(nbytes), "gb_s": gbs, "frac": gbs / hbm}
     assert _lib.device_status() == 0
     cpu = None
-    if not args.no_cpu_baseline:
+    if with_cpu:
         import oracle
 
+        cores = _cpu_threads()
         xn = x.float().cpu().numpy()
         wn = w.cpu().numpy()
         oracle.rmsnorm_fwd(xn, wn, 1e-5, dtype=np.float32)
         t0 = time.perf_counter()
         oracle.rmsnorm_fwd(xn, wn, 1e-5, dtype=np.float32)
         t_cpu = time.perf_counter() - t0
-        cpu = {"value": 2 * T * C * b / t_cpu / 1e9, "unit": "GB/s", "cores": len(os.sched_getaffinity(0)),
+        cpu = {"value": 2 * T * C * b / t_cpu / 1e9, "unit": "GB/s", "cores": cores,
                "kind": "port", "sample": f"rmsnorm_fwd on the full cfg3 batch (fp32 numpy oracle), {t_cpu:.3f} s"}
+    return res, cpu, hbm, kind, T
+
+
+def run_norm_suite(args):
+    import torch
+
+    torch.cuda.set_device(0)
+    res, cpu, hbm, kind, T = measure_norms(args.steps, args.warmup, not args.no_cpu_baseline)
     line = {
         "metric": "varlen norms / softmax / gathers HBM GB/s (cfg3)",
         "value": res["rmsnorm_fwd"]["gb_s"],
@@ -344,7 +383,7 @@ def run_norm_suite(args):
         "higher_is_better": True,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": f"cfg3: 64 seqs lognormal(ln 256, 0.6) seed 0, T={T}, hidden {C} bf16",
+        "config": {"workload": f"cfg3: 64 seqs lognormal(ln 256, 0.6) seed 0, T={T}, hidden 4096 bf16",
                    "l2": "256 MB buffer written before every timed call", "timing": "kernel time from CUDA events around each launch inside libscree_b200 (all launches of the call summed)"},
         "ops": res,
         "hbm_peak_gbs": hbm,
@@ -358,13 +397,15 @@ def run_norm_suite(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--config", default="cfg4", choices=["cfg4", "cfg2", "cfg5"])
     ap.add_argument("--e2e-steps", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-norms", action="store_true", help="skip the cfg3 norms/softmax/gathers object")
+    ap.add_argument("--no-gather", action="store_true", help="N>1: skip the with-output-exchange timing")
     ap.add_argument("--non-causal", action="store_true")
     ap.add_argument("--shard", choices=["seqs", "heads"], default="seqs",
                     help="multi-GPU split: whole sequences (default) or sequences split by head groups")
@@ -415,6 +456,7 @@ def main():
         groups = [(hs, [lengths[u.seq] for u in us])
                   for hs, us in sorted(shard.units_by_heads(plan[rank]).items(), reverse=True)]
         args.no_e2e = True  # the end-to-end path is measured on whole sequences
+        args.no_gather = True
     else:
         plan = shard.plan_shards(lengths, world, cost="attention")
         if world > 1:
@@ -448,12 +490,20 @@ def main():
             out.backward(dog)
 
     tensor_bytes = sum(qg.numel() for qg, *_ in calls) * q.element_size()
-    flush = None
-    if tensor_bytes < L2_FLUSH_BYTES:
-        flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    args.l2_note = (f"inputs larger than L2 (each of q/k/v/dO {tensor_bytes / 1e6:.0f} MB per rank)"
-                    if flush is None else
-                    f"q/k/v/dO {tensor_bytes / 1e6:.0f} MB each per rank: 256 MB buffer written before every timed step, outside its events")
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    args.l2_note = (f"q/k/v/dO {tensor_bytes / 1e6:.0f} MB each per rank; a 256 MB buffer is written "
+                    f"before every timed step, outside its CUDA events (same at every N)")
+
+    def timed_steps(n, fn):
+        """Sum of per-step CUDA-event times of n steps, L2 flushed before each."""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for a, b in evs:
+            flush.fill_(1)
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -468,27 +518,7 @@ def main():
     _lib.profile_read(_lib.PROF_ATTN_BWD)
     _lib.profile_enable(True)
     n0 = _lib.launch_count()
-    if flush is None:
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        ev0.record()
-        for _ in range(args.steps):
-            step()
-        ev1.record()
-        torch.cuda.synchronize()
-        elapsed_ms = ev0.elapsed_time(ev1)
-    else:
-        # Inputs fit in L2: a 256 MB buffer is written before every step, outside
-        # that step's event pair; the steps' own device times are summed.
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
-        for a, b in evs:
-            flush.fill_(1)
-            a.record()
-            step()
-            b.record()
-        torch.cuda.synchronize()
-        elapsed_ms = sum(a.elapsed_time(b) for a, b in evs)
+    elapsed_ms = timed_steps(args.steps, step)
     launches = _lib.launch_count() - n0
     _lib.profile_enable(False)
     fwd_ms, nf = _lib.profile_read(_lib.PROF_ATTN_FWD)
@@ -497,6 +527,39 @@ def main():
         dist.barrier()
     sampler.stop()
     assert _lib.device_status() == 0, "kernel reported an error (device status word)"
+
+    # ------------------------------------------------------------ with output exchange
+    with_gather = None
+    if world > 1 and args.shard == "seqs" and not args.no_gather:
+        offs_g = np.concatenate([[0], np.cumsum(lengths)])
+        mine = shard.local_shard(offs_g, plan, rank)
+        T_all = int(offs_g[-1])
+
+        def step_gather():
+            for t in (q, k, v):
+                t.grad = None
+            out = varlen_attention_triton_autograd(q, k, v, cu, causal=causal)
+            out.backward(do)
+            for t in (out.detach(), q.grad, k.grad, v.grad):
+                shard.gather_to_rank0(t, mine, T_all, plan=plan, global_offsets=offs_g)
+
+        for _ in range(2):
+            step_gather()
+        torch.cuda.synchronize()
+        dist.barrier()
+        g_steps = max(3, min(args.steps, 20))
+        g_ms = timed_steps(g_steps, step_gather)
+        gm = torch.tensor([g_ms / g_steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(gm, op=dist.ReduceOp.MAX)
+        recv_bytes = 4 * (T_all - mine.tokens) * H * D * q.element_size()
+        with_gather = {
+            "ms_per_step": float(gm[0]),
+            "steps": g_steps,
+            "value": float(sum(lengths)) / (float(gm[0]) / 1e3),
+            "unit": "tokens/s",
+            "collective": "NCCL send/recv of every rank's O, dQ, dK, dV rows to rank 0 (batched P2P over NVLink) after each step's backward",
+            "bytes_into_rank0_per_step": int(recv_bytes),
+        }
 
     flops_mine = sum(workloads.attn_flops(ls, hs, D, causal) for hs, ls in groups)
     flops_fwd_mine = sum(workloads.attn_flops(ls, hs, D, causal, fwd=True, bwd=False) for hs, ls in groups)
@@ -515,20 +578,18 @@ def main():
     tflops = total_flops / (ms_step / 1e3) / 1e12
 
     peaks, peak_kind = load_peaks()
-    peak_tf = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    # The burst GEMM figure is the denominator: these kernels run at the
+    # unthrottled clock (see "clocks"), where the sustained figure was measured
+    # under the power cap at a lower clock.  frac_of_sustained is given too.
+    peak_tf = float(peaks.get("bf16_tflops", peaks.get("bf16_tflops_sustained")))
+    peak_sus = float(peaks.get("bf16_tflops_sustained", peak_tf))
     bwd_avg_ms = bwd_ms / max(nb, 1)
     fwd_avg_ms = fwd_ms / max(nf, 1)
     # This rank's FLOPs per step over its kernel time per step (one launch per
     # step and kind, or one per head-count group with --shard heads).
     ach_bwd = flops_bwd_mine / (bwd_ms / args.steps / 1e3) / 1e12
     ach_fwd = flops_fwd_mine / (fwd_ms / args.steps / 1e3) / 1e12
-    traffic = None
-    tp = ROOT / "profiles" / "attn_bwd_cfg4_traffic.json"
-    if tp.exists():
-        try:
-            traffic = json.loads(tp.read_text()).get("bytes_per_launch")
-        except Exception:
-            traffic = None
+    traffic, traffic_src = scaled_traffic(groups, D, causal)
 
     # ------------------------------------------------------------ end to end
     e2e = None
@@ -602,6 +663,18 @@ def main():
         rate, cores, sample = cpu_reference_rate(lengths, H, D, causal)
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
 
+    norms = None
+    if world == 1 and not args.no_norms:
+        nres, ncpu, hbm, nkind, nT = measure_norms(max(10, min(args.steps, 30)), args.warmup, not args.no_cpu_baseline)
+        norms = {
+            "workload": f"cfg3: 64 seqs lognormal(ln 256, 0.6) seed 0, T={nT}, hidden 4096 bf16; L2 flushed before each launch",
+            "hbm_peak_gbs": hbm,
+            "peak_source": f"{nkind} hbm_gbs",
+            "ops": {k_: {"gb_s": round(v_["gb_s"], 1), "frac": round(v_["frac"], 4), "ms": v_["ms"],
+                         "algorithmic_bytes": v_["algorithmic_bytes"]} for k_, v_ in nres.items()},
+            "cpu_baseline": ncpu,
+        }
+
     if rank == 0:
         line = {
             "metric": METRIC,
@@ -619,6 +692,7 @@ def main():
             "config": workload_config(args, lengths, H, D, causal, world),
             "tflops": tflops,
             "tflops_frac_of_peak": tflops / (peak_tf * world),
+            "tflops_frac_of_sustained_peak": tflops / (peak_sus * world),
             "roofline": {
                 "kernel": "attn_bwd_kernel<128, bf16, causal> (dK/dV/dQ, 10*H*D*pairs FLOPs)",
                 "bound": "tensor",
@@ -626,14 +700,20 @@ def main():
                 "peak": peak_tf,
                 "unit": "TFLOP/s",
                 "frac": ach_bwd / peak_tf,
-                "peak_source": f"{peak_kind} bf16_tflops_sustained (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 1.4 PFLOP/s sustained",
+                "frac_of_sustained_peak": ach_bwd / peak_sus,
+                "peak_source": (f"{peak_kind} bf16_tflops (burst, MEASURED_PEAKS.json)" if peak_kind == "measured"
+                                else "fallback 1.59 PFLOP/s burst"),
                 "traffic": traffic,
+                "traffic_source": traffic_src,
                 "avg_launch_ms": bwd_avg_ms,
             },
             "kernels": {
                 "attn_fwd": {"avg_ms": fwd_avg_ms, "launches": nf, "tflops": ach_fwd, "frac": ach_fwd / peak_tf},
                 "attn_bwd": {"avg_ms": bwd_avg_ms, "launches": nb, "tflops": ach_bwd, "frac": ach_bwd / peak_tf},
             },
+            "compute_only_ms": ms_step,
+            "with_gather": with_gather,
+            "norms": norms,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(total_launch),

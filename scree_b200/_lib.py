@@ -14,6 +14,7 @@ import os
 
 # SCREE_B200_LIB points at another build of the library (benchmark A/B runs).
 LIB_PATH = Path(os.environ.get("SCREE_B200_LIB", Path(__file__).resolve().parent / "libscree_b200.so"))
+_ALT_LIB = "SCREE_B200_LIB" in os.environ
 
 SCREE_OK = 0
 SCREE_ERR_INVALID = 1
@@ -62,6 +63,8 @@ _SIGNATURES = {
     "scree_pack": (_I, [_P, _P, _I, _L, _L, _L, _L, _L, _P, _P]),
     "scree_to_padded": (_I, [_P, _P, _I, _L, _L, _L, _L, _P, _I, _P, _P, _P]),
     "scree_padded_lengths": (_I, [_P, _L, _L, _P, _P]),
+    "scree_padded_lengths_ex": (_I, [_P, _I, _L, _L, _P, _P]),
+    "scree_to_padded_ex": (_I, [_P, _P, _I, _L, _L, _L, _L, _P, _I, _P, _P, _I, _P]),
     "scree_from_padded": (_I, [_P, _P, _L, _L, _L, _L, _P, _P]),
 }
 
@@ -89,6 +92,8 @@ def load() -> ctypes.CDLL:
                 )
             lib = ctypes.CDLL(str(LIB_PATH))
             for name, (res, args) in _SIGNATURES.items():
+                if _ALT_LIB and not hasattr(lib, name):
+                    continue  # an older build under A/B comparison may lack newer entry points
                 fn = getattr(lib, name)
                 fn.restype = res
                 fn.argtypes = args
