@@ -105,6 +105,18 @@ int scree_attn_fwd(const void* q, const void* k, const void* v, int64_t q_row_st
                    int64_t o_head_stride, float* lse, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* Grouped-query attention forward: q (T, H, D) with H = H_kv * G query heads,
+ * k and v (T, H_kv, D); query head h reads K / V head h / G.  Otherwise as
+ * scree_attn_fwd (which is this call with H_kv = H).  The reference lists GQA
+ * as not yet supported (docs/kernels.md:177); no reference counterpart. */
+int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, int64_t q_row_stride,
+                       int64_t q_head_stride, int64_t k_row_stride, int64_t k_head_stride,
+                       int64_t v_row_stride, int64_t v_head_stride, const void* offsets,
+                       int offs_is_i64, int64_t B, int64_t T, int64_t H, int64_t H_kv, int D,
+                       int dtype, int causal, float scale, int64_t max_seqlen, void* o,
+                       int64_t o_row_stride, int64_t o_head_stride, float* lse, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of scree_attn_fwd (no counterpart in the reference).
  * For callers that cannot allocate device memory when they run attention (an
  * engine with a fixed pre-planned memory arena, or a binding that only holds
@@ -138,6 +150,16 @@ int scree_attn_bwd(const void* dout, const void* q, const void* k, const void* v
                    int64_t H, int D, int dtype, int causal, float scale, int64_t max_seqlen,
                    void* dq, void* dk, void* dv, void* workspace, size_t workspace_bytes,
                    void* stream);
+
+/* Grouped-query attention backward: dq (T, H, D); dk, dv (T, H_kv, D) summed
+ * over the G query heads that share each K / V head.  Contiguous tensors as in
+ * scree_attn_bwd (= this call with H_kv = H); same workspace size (H = query
+ * heads).  No reference counterpart (docs/kernels.md:177). */
+int scree_attn_bwd_gqa(const void* dout, const void* q, const void* k, const void* v,
+                       const void* o, const float* lse, const void* offsets, int offs_is_i64,
+                       int64_t B, int64_t T, int64_t H, int64_t H_kv, int D, int dtype, int causal,
+                       float scale, int64_t max_seqlen, void* dq, void* dk, void* dv,
+                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------ norms
  * RMSNorm forward over the last dim of a (rows, C) row-major buffer.
@@ -208,11 +230,26 @@ int scree_to_padded(const void* values, const void* offsets, int offs_is_i64, in
                     const void* fill_pattern_host, int side_left, void* padded, uint8_t* mask,
                     void* stream);
 
+/* to_padded with the mask written in an integer width of 1, 2, 4 or 8 bytes
+ * (1 / 0 per position): the HF attention_mask convention is int64.
+ * Replaces: scree/bridges/_hf_padded.py:32-46 to_hf_padded (to_padded, then a
+ * mask dtype conversion) with one kernel.  Otherwise as scree_to_padded. */
+int scree_to_padded_ex(const void* values, const void* offsets, int offs_is_i64, int64_t B,
+                       int64_t max_len, int64_t row_bytes, int64_t elem_bytes,
+                       const void* fill_pattern_host, int side_left, void* padded, void* mask,
+                       int mask_elem_bytes, void* stream);
+
 /* from_padded, step 1: per-row lengths = mask.sum(1) and int32 offsets (B+1,).
  * Replaces: scree/_core.py:253-301 from_padded (torch branch :260-267), which
  * assumes right padding. */
 int scree_padded_lengths(const uint8_t* mask, int64_t B, int64_t max_len, int32_t* offsets_out,
                          void* stream);
+/* Step 1 for a mask of 1-, 2-, 4- or 8-byte integers (nonzero = valid), read
+ * as is: the HF attention_mask is int64.
+ * Replaces: scree/bridges/_hf_padded.py:15-29 from_hf_padded (mask cast to bool,
+ * then from_padded). */
+int scree_padded_lengths_ex(const void* mask, int mask_elem_bytes, int64_t B, int64_t max_len,
+                            int32_t* offsets_out, void* stream);
 /* from_padded, step 2: gather the first lengths[b] rows of each padded row into
  * the packed (T, ...) buffer, using the offsets from step 1. */
 int scree_from_padded(const void* padded, const int32_t* offsets, int64_t B, int64_t max_len,

@@ -254,6 +254,13 @@ def to_padded(arr: Array, side: str = "right", fill_value: float = 0.0) -> Tuple
     """
     import torch
 
+    return _to_padded_mask(arr, side, fill_value, torch.bool)
+
+
+def _to_padded_mask(arr: Array, side: str, fill_value: float, mask_dtype) -> Tuple[Any, Any]:
+    """to_padded with the mask written as `mask_dtype` (bool or an integer type)."""
+    import torch
+
     if arr.ragged_dim != 0:
         raise NotImplementedError("to_padded supports ragged_dim=0 only in v0.1")
     if side not in ("right", "left"):
@@ -267,7 +274,7 @@ def to_padded(arr: Array, side: str = "right", fill_value: float = 0.0) -> Tuple
     feat = tuple(vals.shape[1:])
     dev = vals.device
     padded = torch.empty((B, max_len, *feat), dtype=vals.dtype, device=dev)
-    mask = torch.empty((B, max_len), dtype=torch.bool, device=dev)
+    mask = torch.empty((B, max_len), dtype=mask_dtype, device=dev)
     offs = arr.offsets
     if not (_is_torch(offs) and offs.device == dev):
         offs = torch.as_tensor(host, dtype=torch.int64, device=dev)
@@ -279,10 +286,10 @@ def to_padded(arr: Array, side: str = "right", fill_value: float = 0.0) -> Tuple
     buf = ctypes_buffer(pat)
     if B and max_len:
         with torch.cuda.device(dev):
-            rc = _lib.load().scree_to_padded(
+            rc = _lib.load().scree_to_padded_ex(
                 vals.data_ptr(), offs.data_ptr(), 1 if offs.dtype == torch.int64 else 0,
                 B, max_len, row_bytes, vals.element_size(), buf, 1 if side == "left" else 0,
-                padded.data_ptr(), mask.data_ptr(), _lib.stream_ptr(dev),
+                padded.data_ptr(), mask.data_ptr(), mask.element_size(), _lib.stream_ptr(dev),
             )
         _lib.check(rc, "scree_to_padded")
     return padded, mask
@@ -302,11 +309,18 @@ def from_padded(padded: Any, mask: Any) -> Array:
     import torch
 
     _require_cuda(padded, "from_padded")
+    return _from_padded_mask(padded, mask.to(device=padded.device, dtype=torch.bool).contiguous())
+
+
+def _from_padded_mask(padded: Any, m: Any) -> Array:
+    """from_padded with a contiguous device mask of bool or 1/2/4/8-byte
+    integers (nonzero = valid), read in its own width."""
+    import torch
+
     B = int(padded.shape[0])
     max_len = int(padded.shape[1]) if padded.ndim > 1 else 0
     dev = padded.device
     pad = padded.contiguous()
-    m = mask.to(device=dev, dtype=torch.bool).contiguous()
     offsets = torch.empty(B + 1, dtype=torch.int32, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
@@ -314,7 +328,8 @@ def from_padded(padded: Any, mask: Any) -> Array:
             offsets.zero_()
         else:
             _lib.check(
-                lib.scree_padded_lengths(m.data_ptr(), B, max_len, offsets.data_ptr(), _lib.stream_ptr(dev)),
+                lib.scree_padded_lengths_ex(m.data_ptr(), m.element_size(), B, max_len, offsets.data_ptr(),
+                                            _lib.stream_ptr(dev)),
                 "scree_padded_lengths",
             )
         host = [int(v) for v in offsets.tolist()]  # the one sync: T sizes the output

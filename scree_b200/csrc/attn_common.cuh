@@ -93,11 +93,11 @@ int make_thd_map_f32(CUtensorMap* map, const void* base, int64_t T, int64_t H, i
 // fp32 attention (attn_f32.cu): CUDA-core kernels for fp32 inputs.
 int attn_fwd_f32(const void* q, const void* k, const void* v, int64_t q_rs, int64_t q_hs,
                  int64_t k_rs, int64_t k_hs, int64_t v_rs, int64_t v_hs, const void* offsets,
-                 int is64, int64_t B, int64_t T, int64_t H, int D, int causal, float scale,
-                 void* o, int64_t o_rs, int64_t o_hs, float* lse, cudaStream_t s);
+                 int is64, int64_t B, int64_t T, int64_t H, int64_t H_kv, int D, int causal,
+                 float scale, void* o, int64_t o_rs, int64_t o_hs, float* lse, cudaStream_t s);
 int attn_bwd_f32(const void* dout, const void* q, const void* k, const void* v, const void* o,
                  const float* lse, const void* offsets, int is64, int64_t B, int64_t T, int64_t H,
-                 int D, int causal, float scale, void* dq, void* dk, void* dv, float* delta,
-                 cudaStream_t s);
+                 int64_t H_kv, int D, int causal, float scale, void* dq, void* dk, void* dv,
+                 float* delta, cudaStream_t s);
 
 }  // namespace scree

@@ -18,6 +18,8 @@
 //             O = P V / l, LSE = m + ln l (natural log, like the 16-bit path)
 //   backward  pass 1, warp = query row: Delta = O.dO, dQ = scale * sum_k dS K;
 //             pass 2, warp = key row:   dV = sum_q P dO, dK = scale * sum_q dS Q
+//             (grouped-query attention: over the queries of every query head
+//             that shares the key's K / V head)
 //             with P = exp(S - LSE), dS = P (dO.V - Delta); no atomics, so the
 //             result is deterministic.
 #include "attn_common.cuh"
@@ -67,6 +69,7 @@ struct F32Params {
   int is64;
   int64_t B, T;
   int H;
+  int G;  // query heads per K / V head
   int causal;
   float scale;
   float* o;
@@ -102,8 +105,8 @@ __global__ void __launch_bounds__(kWarps * 32) attn_fwd_f32_kernel(const F32Para
     for (int u = 0; u < 4; ++u) {
       if (j + u < kend) {
         Row<D> kr;
-        kr.load(p.k + (j + u) * p.k_rs + h * p.k_hs, lane);
-        vr[u].load(p.v + (j + u) * p.v_rs + h * p.v_hs, lane);
+        kr.load(p.k + (j + u) * p.k_rs + (h / p.G) * p.k_hs, lane);
+        vr[u].load(p.v + (j + u) * p.v_rs + (h / p.G) * p.v_hs, lane);
         s[u] = q.dot(kr);
       } else {
         s[u] = 0.f;
@@ -142,7 +145,9 @@ struct F32BwdParams {
   const void* offs;
   int is64;
   int64_t B, T;
-  int H;
+  int H;    // query heads
+  int Hkv;  // K / V heads (H = Hkv * G)
+  int G;
   int causal;
   float scale;
   float* delta;  // (T, H) workspace
@@ -183,8 +188,8 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_f32_dq_kernel(const F32B
     for (int u = 0; u < 4; ++u) {
       if (j + u < kend) {
         Row<D> vr;
-        kr[u].load(p.k + ((j + u) * p.H + h) * D, lane);
-        vr.load(p.v + ((j + u) * p.H + h) * D, lane);
+        kr[u].load(p.k + ((j + u) * p.Hkv + h / p.G) * D, lane);
+        vr.load(p.v + ((j + u) * p.Hkv + h / p.G) * D, lane);
         s[u] = q.dot(kr[u]);
         dp[u] = dO.dot(vr);
       } else {
@@ -215,22 +220,25 @@ template <int D>
 __global__ void __launch_bounds__(kWarps * 32) attn_bwd_f32_dkv_kernel(const F32BwdParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t w = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5);
-  if (w >= p.T * p.H) return;
-  const int h = (int)(w / p.T);
-  const int64_t t = w % p.T;  // the key row
+  if (w >= p.T * p.Hkv) return;
+  const int h = (int)(w / p.T);  // K / V head
+  const int64_t t = w % p.T;     // the key row
   const int64_t b = find_seq(p.offs, p.is64, p.B, t);
   const int64_t s0 = load_offset(p.offs, p.is64, b), s1 = load_offset(p.offs, p.is64, b + 1);
   if (t < s0 || t >= s1 || s0 < 0 || s1 > p.T) {
     if (lane == 0) record_device_error(p.status, SCREE_DEVERR_BAD_INPUT, 46);
     return;
   }
-  const int64_t row = (t * p.H + h) * D;
+  const int64_t row = (t * p.Hkv + h) * D;
   Row<D> kr, vr;
   kr.load(p.k + row, lane);
   vr.load(p.v + row, lane);
   Row<D> dk, dv;
 #pragma unroll
   for (int i = 0; i < Row<D>::N; ++i) dk.x[i] = dv.x[i] = 0.f;
+  // Every query of the sequence (causal: from t on) of every query head of the group.
+  for (int g = 0; g < p.G; ++g) {
+  const int hq = h * p.G + g;
   for (int64_t i0 = p.causal ? t : s0; i0 < s1; i0 += 4) {
     float s[4], dp[4], lse[4], del[4];
     Row<D> qr[4], dor[4];
@@ -238,12 +246,12 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_f32_dkv_kernel(const F32
     for (int u = 0; u < 4; ++u) {
       const int64_t qi = i0 + u;
       if (qi < s1) {
-        qr[u].load(p.q + (qi * p.H + h) * D, lane);
-        dor[u].load(p.dout + (qi * p.H + h) * D, lane);
+        qr[u].load(p.q + (qi * p.H + hq) * D, lane);
+        dor[u].load(p.dout + (qi * p.H + hq) * D, lane);
         s[u] = qr[u].dot(kr);
         dp[u] = dor[u].dot(vr);
-        lse[u] = p.lse[qi * p.H + h];
-        del[u] = p.delta[qi * p.H + h];
+        lse[u] = p.lse[qi * p.H + hq];
+        del[u] = p.delta[qi * p.H + hq];
       } else {
         s[u] = dp[u] = lse[u] = del[u] = 0.f;
 #pragma unroll
@@ -266,6 +274,7 @@ __global__ void __launch_bounds__(kWarps * 32) attn_bwd_f32_dkv_kernel(const F32
       }
     }
   }
+  }
 #pragma unroll
   for (int i = 0; i < Row<D>::N; ++i) {
     p.dv[row + lane + 32 * i] = dv.x[i];
@@ -281,11 +290,12 @@ inline unsigned warps_grid(int64_t T, int64_t H) {
 
 int attn_fwd_f32(const void* q, const void* k, const void* v, int64_t q_rs, int64_t q_hs,
                  int64_t k_rs, int64_t k_hs, int64_t v_rs, int64_t v_hs, const void* offsets,
-                 int is64, int64_t B, int64_t T, int64_t H, int D, int causal, float scale,
-                 void* o, int64_t o_rs, int64_t o_hs, float* lse, cudaStream_t s) {
+                 int is64, int64_t B, int64_t T, int64_t H, int64_t H_kv, int D, int causal,
+                 float scale, void* o, int64_t o_rs, int64_t o_hs, float* lse, cudaStream_t s) {
   SCREE_CHECK_ARG(T * H / kWarps < (1ll << 31), "attn_fwd (fp32): T x H too large");
   F32Params p{(const float*)q, (const float*)k, (const float*)v, q_rs, q_hs, k_rs, k_hs, v_rs,
-              v_hs, offsets, is64, B, T, (int)H, causal, scale, (float*)o, o_rs, o_hs, lse,
+              v_hs, offsets, is64, B, T, (int)H, (int)(H / H_kv), causal, scale, (float*)o, o_rs,
+              o_hs, lse,
               device_status_ptr()};
   const unsigned grid = warps_grid(T, H);
   ProfScope prof(PROF_ATTN_FWD, s);
@@ -300,18 +310,19 @@ int attn_fwd_f32(const void* q, const void* k, const void* v, int64_t q_rs, int6
 
 int attn_bwd_f32(const void* dout, const void* q, const void* k, const void* v, const void* o,
                  const float* lse, const void* offsets, int is64, int64_t B, int64_t T, int64_t H,
-                 int D, int causal, float scale, void* dq, void* dk, void* dv, float* delta,
-                 cudaStream_t s) {
+                 int64_t H_kv, int D, int causal, float scale, void* dq, void* dk, void* dv,
+                 float* delta, cudaStream_t s) {
   SCREE_CHECK_ARG(T * H / kWarps < (1ll << 31), "attn_bwd (fp32): T x H too large");
   F32BwdParams p{(const float*)q, (const float*)k, (const float*)v, (const float*)o,
-                 (const float*)dout, lse, offsets, is64, B, T, (int)H, causal, scale, delta,
+                 (const float*)dout, lse, offsets, is64, B, T, (int)H, (int)H_kv, (int)(H / H_kv),
+                 causal, scale, delta,
                  (float*)dq, (float*)dk, (float*)dv, device_status_ptr()};
-  const unsigned grid = warps_grid(T, H);
+  const unsigned grid = warps_grid(T, H), grid_kv = warps_grid(T, H_kv);
   ProfScope prof(PROF_ATTN_BWD, s);
 #define SCREE_F32_BWD(DD)                                                   \
   attn_bwd_f32_dq_kernel<DD><<<grid, kWarps * 32, 0, s>>>(p);               \
   SCREE_LAUNCH_CHECK();                                                     \
-  attn_bwd_f32_dkv_kernel<DD><<<grid, kWarps * 32, 0, s>>>(p);              \
+  attn_bwd_f32_dkv_kernel<DD><<<grid_kv, kWarps * 32, 0, s>>>(p);           \
   SCREE_LAUNCH_CHECK();
   switch (D) {
     case 32: SCREE_F32_BWD(32) break;

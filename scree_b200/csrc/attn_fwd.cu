@@ -86,7 +86,8 @@ struct FwdCfg {
 struct FwdParams {
   const void* offs;
   int is64;
-  int H;
+  int H;  // query heads
+  int G;  // query heads per K / V head (grouped-query attention; 1 = plain)
   int T;
   float scale_log2;
   const void* sched;  // schedule (attn_common.cuh)
@@ -225,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ TMA producer
     regs_dec<kRegsOther>();
     const int row0 = (int)seq_start;
+    const int hkv = h / p.G;  // the K / V head this query head reads
     if (lane == 0) {
       mbar_expect_tx(q_full, (hasB ? 2 : 1) * C::Q_BYTES);
       for (int x = 0; x < (hasB ? 2 : 1); ++x)
@@ -241,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c)
           tma_load_3d(smem + C::OFF_K + st * C::KV_BYTES + c * BN * C::SWB, &tm_k, &k_full[st],
-                      c * C::CHUNK, h, row0 + j * BN);
+                      c * C::CHUNK, hkv, row0 + j * BN);
       }
     } else if (lane == 1) {
       for (int j = 0; j < n_kv; ++j) {
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c)
           tma_load_3d(smem + C::OFF_V + st * C::KV_BYTES + c * BN * C::SWB, &tm_v, &v_full[st],
-                      c * C::CHUNK, h, row0 + j * BN);
+                      c * C::CHUNK, hkv, row0 + j * BN);
       }
     }
   } else if (warp == 9) {
@@ -558,7 +560,22 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
                               int64_t T, int64_t H, int D, int dtype, int causal, float scale,
                               int64_t max_seqlen, void* o, int64_t o_rs, int64_t o_hs, float* lse,
                               void* workspace, size_t workspace_bytes, void* stream) {
+  return scree_attn_fwd_gqa(q, k, v, q_rs, q_hs, k_rs, k_hs, v_rs, v_hs, offsets, offs_is_i64, B,
+                            T, H, H, D, dtype, causal, scale, max_seqlen, o, o_rs, o_hs, lse,
+                            workspace, workspace_bytes, stream);
+}
+
+extern "C" int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, int64_t q_rs,
+                                  int64_t q_hs, int64_t k_rs, int64_t k_hs, int64_t v_rs,
+                                  int64_t v_hs, const void* offsets, int offs_is_i64, int64_t B,
+                                  int64_t T, int64_t H, int64_t H_kv, int D, int dtype,
+                                  int causal, float scale, int64_t max_seqlen, void* o,
+                                  int64_t o_rs, int64_t o_hs, float* lse, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
   (void)max_seqlen;
+  SCREE_CHECK_ARG(H_kv >= 1 && H % H_kv == 0,
+                  "attn_fwd: query heads (%lld) must be a multiple of K/V heads (%lld)",
+                  (long long)H, (long long)H_kv);
   SCREE_CHECK_ARG(B >= 1 && T >= 0 && H >= 1, "attn_fwd: bad sizes B=%lld T=%lld H=%lld",
                   (long long)B, (long long)T, (long long)H);
   SCREE_CHECK_ARG(T < (1ll << 31) && H < 65536, "attn_fwd: T or H too large");
@@ -573,7 +590,7 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
   if (dtype == SCREE_F32) {  // CUDA-core fp32 kernels; no workspace needed
     SCREE_BIND_DEVICE(stream, q);
     return attn_fwd_f32(q, k, v, q_rs, q_hs, k_rs, k_hs, v_rs, v_hs, offsets, offs_is_i64, B, T,
-                        H, D, causal, scale, o, o_rs, o_hs, lse, (cudaStream_t)stream);
+                        H, H_kv, D, causal, scale, o, o_rs, o_hs, lse, (cudaStream_t)stream);
   }
   SCREE_CHECK_ARG(workspace && workspace_bytes >= schedule_bytes(B),
                   "attn_fwd: workspace too small");
@@ -586,13 +603,14 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
   CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_thd_map(&tq, q, T, H, D, q_rs, q_hs, swb / 2, BM, swb, bf16))) return rc;
-  if ((rc = make_thd_map(&tk, k, T, H, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
-  if ((rc = make_thd_map(&tv, v, T, H, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tk, k, T, H_kv, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tv, v, T, H_kv, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
   if ((rc = launch_build_schedule(offsets, offs_is_i64, B, T, ROWS, (int)H, workspace, s))) return rc;
   FwdParams p;
   p.offs = offsets;
   p.is64 = offs_is_i64;
   p.H = (int)H;
+  p.G = (int)(H / H_kv);
   p.T = (int)T;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.sched = workspace;

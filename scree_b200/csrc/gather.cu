@@ -62,7 +62,7 @@ template <int W>
 __global__ void __launch_bounds__(kThreads) to_padded_kernel(
     const void* __restrict__ values, const void* offs, int is64, int64_t B, int64_t max_len,
     int64_t row_bytes, int rows_per_cta, uint4 fill16, int side_left, void* __restrict__ padded,
-    uint8_t* __restrict__ mask, int* status) {
+    void* __restrict__ mask, int mask_bytes, int* status) {
   using V = typename Vec<W>::T;
   V fill;
   memcpy(&fill, &fill16, sizeof(V));
@@ -91,14 +91,22 @@ __global__ void __launch_bounds__(kThreads) to_padded_kernel(
     if (mask != nullptr)
       for (uint32_t r = threadIdx.x; r < nrows; r += blockDim.x) {
         const int64_t src_row = j0 + r - shift;
-        mask[b * max_len + j0 + r] = (src_row >= 0 && src_row < len) ? 1 : 0;
+        const int on = (src_row >= 0 && src_row < len) ? 1 : 0;
+        const int64_t mi = b * max_len + j0 + r;
+        switch (mask_bytes) {  // bool / uint8, int16, int32 or int64 (HF) masks
+          case 8: reinterpret_cast<int64_t*>(mask)[mi] = on; break;
+          case 4: reinterpret_cast<int32_t*>(mask)[mi] = on; break;
+          case 2: reinterpret_cast<int16_t*>(mask)[mi] = (int16_t)on; break;
+          default: reinterpret_cast<uint8_t*>(mask)[mi] = (uint8_t)on; break;
+        }
       }
   }
 }
 
 // ---------------------------------------------------------------- from_padded
 // Step 1a: one CTA per padded row writes its mask count into offsets[b+1].
-__global__ void padded_count_kernel(const uint8_t* __restrict__ mask, int64_t max_len,
+template <typename MT>
+__global__ void padded_count_kernel(const MT* __restrict__ mask, int64_t max_len,
                                     int32_t* __restrict__ offsets) {
   __shared__ int red[32];
   const int64_t b = blockIdx.x;
@@ -218,6 +226,18 @@ extern "C" int scree_to_padded(const void* values, const void* offsets, int offs
                                int64_t B, int64_t max_len, int64_t row_bytes, int64_t elem_bytes,
                                const void* fill_pattern_host, int side_left, void* padded,
                                uint8_t* mask, void* stream) {
+  return scree_to_padded_ex(values, offsets, offs_is_i64, B, max_len, row_bytes, elem_bytes,
+                            fill_pattern_host, side_left, padded, mask, 1, stream);
+}
+
+extern "C" int scree_to_padded_ex(const void* values, const void* offsets, int offs_is_i64,
+                                  int64_t B, int64_t max_len, int64_t row_bytes,
+                                  int64_t elem_bytes, const void* fill_pattern_host,
+                                  int side_left, void* padded, void* mask, int mask_elem_bytes,
+                                  void* stream) {
+  SCREE_CHECK_ARG(mask_elem_bytes == 1 || mask_elem_bytes == 2 || mask_elem_bytes == 4 ||
+                      mask_elem_bytes == 8,
+                  "scree_to_padded: mask elements must be 1, 2, 4 or 8 bytes");
   SCREE_CHECK_ARG(B >= 0 && max_len >= 0 && row_bytes >= 0, "scree_to_padded: bad sizes");
   SCREE_CHECK_ARG(elem_bytes == 1 || elem_bytes == 2 || elem_bytes == 4 || elem_bytes == 8,
                   "scree_to_padded: elem_bytes must be 1, 2, 4 or 8");
@@ -244,10 +264,11 @@ extern "C" int scree_to_padded(const void* values, const void* offsets, int offs
   if (row_bytes == 0) {
     to_padded_kernel<1><<<grid, kThreads, 0, s>>>(values, offsets, offs_is_i64, B, max_len, 0,
                                                    rpc, fill16, side_left, nullptr, mask,
-                                                   device_status_ptr());
+                                                   mask_elem_bytes, device_status_ptr());
   } else {
     DISPATCH_WIDTH(w, to_padded_kernel, grid, s, values, offsets, offs_is_i64, B, max_len,
-                   row_bytes, rpc, fill16, side_left, padded, mask, device_status_ptr());
+                   row_bytes, rpc, fill16, side_left, padded, mask, mask_elem_bytes,
+                   device_status_ptr());
   }
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
@@ -255,6 +276,14 @@ extern "C" int scree_to_padded(const void* values, const void* offsets, int offs
 
 extern "C" int scree_padded_lengths(const uint8_t* mask, int64_t B, int64_t max_len,
                                     int32_t* offsets_out, void* stream) {
+  return scree_padded_lengths_ex(mask, 1, B, max_len, offsets_out, stream);
+}
+
+extern "C" int scree_padded_lengths_ex(const void* mask, int mask_elem_bytes, int64_t B,
+                                       int64_t max_len, int32_t* offsets_out, void* stream) {
+  SCREE_CHECK_ARG(mask_elem_bytes == 1 || mask_elem_bytes == 2 || mask_elem_bytes == 4 ||
+                      mask_elem_bytes == 8,
+                  "scree_padded_lengths: mask elements must be 1, 2, 4 or 8 bytes");
   SCREE_CHECK_ARG(B >= 1 && max_len >= 0, "scree_padded_lengths: bad sizes");
   SCREE_CHECK_ARG(offsets_out != nullptr, "scree_padded_lengths: null offsets");
   SCREE_CHECK_ARG(B < (1ll << 31), "scree_padded_lengths: batch too large");
@@ -265,7 +294,20 @@ extern "C" int scree_padded_lengths(const uint8_t* mask, int64_t B, int64_t max_
     return SCREE_OK;
   }
   SCREE_CHECK_ARG(mask != nullptr, "scree_padded_lengths: null mask");
-  padded_count_kernel<<<(unsigned)B, 256, 0, s>>>(mask, max_len, offsets_out);
+  switch (mask_elem_bytes) {  // a nonzero element marks a valid position
+    case 8:
+      padded_count_kernel<<<(unsigned)B, 256, 0, s>>>((const uint64_t*)mask, max_len, offsets_out);
+      break;
+    case 4:
+      padded_count_kernel<<<(unsigned)B, 256, 0, s>>>((const uint32_t*)mask, max_len, offsets_out);
+      break;
+    case 2:
+      padded_count_kernel<<<(unsigned)B, 256, 0, s>>>((const uint16_t*)mask, max_len, offsets_out);
+      break;
+    default:
+      padded_count_kernel<<<(unsigned)B, 256, 0, s>>>((const uint8_t*)mask, max_len, offsets_out);
+      break;
+  }
   SCREE_LAUNCH_CHECK();
   inplace_scan_kernel<<<1, 1024, 0, s>>>(offsets_out, B);
   SCREE_LAUNCH_CHECK();

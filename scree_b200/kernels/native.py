@@ -48,6 +48,14 @@ def _offsets_arg(cu_seqlens: torch.Tensor, device) -> tuple[torch.Tensor, int]:
     return cu, 1 if cu.dtype == torch.int64 else 0
 
 
+def _check_qkv_shapes(q, k, v):
+    assert k.shape == v.shape, "k and v must have identical shape"
+    assert q.ndim == 3 and q.shape[0] == k.shape[0] and q.shape[2] == k.shape[2], \
+        "q, k, v must have identical shape (up to grouped K/V heads)"
+    assert k.shape[1] >= 1 and q.shape[1] % k.shape[1] == 0, \
+        "the query head count must be a multiple of the K/V head count"
+
+
 def _attn_view(t: torch.Tensor) -> torch.Tensor:
     """A (T, H, D) view the TMA tensor maps accept: unit inner stride, 16-byte
     aligned base and row/head strides that are multiples of 8 elements."""
@@ -79,8 +87,10 @@ def varlen_attention_triton(
     {32, 64, 128}.  cu_seqlens: (batch+1,) int32 or int64 offsets.  Returns ``out``
     or ``(out, lse)`` with lse (total_tokens, n_heads) fp32 in natural log.
     ``max_seqlen`` is optional and unused (no host synchronisation is needed).
+    Grouped-query attention: k and v may have fewer heads than q (a divisor of
+    q's head count); query head h then reads K / V head h // (n_heads / kv_heads).
     """
-    assert q.shape == k.shape == v.shape, "q, k, v must have identical shape"
+    _check_qkv_shapes(q, k, v)
     assert q.is_cuda, "varlen_attention_triton requires CUDA tensors"
     assert q.dtype in (torch.float16, torch.bfloat16), "fp16 or bf16 only in v0.0"
     assert k.dtype == q.dtype and v.dtype == q.dtype, "q, k, v must share a dtype"
@@ -101,16 +111,17 @@ def varlen_attention_triton(
     if total == 0:
         return (out, lse) if return_lse else out
     qv, kv, vv = _attn_view(q), _attn_view(k), _attn_view(v)
+    kv_heads = k.shape[1]
     o_direct = out.stride(2) == 1 and out.stride(0) % 8 == 0 and out.stride(1) % 8 == 0 and out.data_ptr() % 16 == 0
     o_buf = out if o_direct else torch.empty_like(q, memory_format=torch.contiguous_format)
     lib = _lib.load()
     ws = torch.empty(lib.scree_attn_fwd_workspace_size(batch, total, n_heads, head_dim), dtype=torch.uint8, device=q.device)
     scale = 1.0 / math.sqrt(head_dim)
     with torch.cuda.device(q.device):
-        rc = lib.scree_attn_fwd(
+        rc = lib.scree_attn_fwd_gqa(
             qv.data_ptr(), kv.data_ptr(), vv.data_ptr(),
             qv.stride(0), qv.stride(1), kv.stride(0), kv.stride(1), vv.stride(0), vv.stride(1),
-            cu.data_ptr(), is64, batch, total, n_heads, head_dim, _lib.dtype_code(q.dtype),
+            cu.data_ptr(), is64, batch, total, n_heads, kv_heads, head_dim, _lib.dtype_code(q.dtype),
             1 if causal else 0, scale, int(max_seqlen or 0),
             o_buf.data_ptr(), o_buf.stride(0), o_buf.stride(1), lse.data_ptr(),
             ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device),
@@ -128,9 +139,11 @@ def varlen_attention_triton_backward(
 
     One sm_100a kernel computes all three gradients per 128-key tile (five GEMMs,
     none recomputed), after a Delta = rowsum(O * dO) pass; dq is accumulated in
-    fp32 and cast once at the end.
+    fp32 and cast once at the end.  With grouped-query k / v (fewer heads), dk
+    and dv have k's shape and sum over the query heads sharing each K / V head.
     """
-    assert q.shape == k.shape == v.shape == o.shape == do.shape, "shape mismatch"
+    _check_qkv_shapes(q, k, v)
+    assert q.shape == o.shape == do.shape, "shape mismatch"
     assert q.is_cuda, "varlen_attention_triton_backward requires CUDA tensors"
     assert q.dtype in (torch.float16, torch.bfloat16), "fp16 or bf16 only in v0.0"
     total, n_heads, head_dim = q.shape
@@ -148,9 +161,9 @@ def varlen_attention_triton_backward(
     ws = torch.empty(lib.scree_attn_bwd_workspace_size(batch, total, n_heads, head_dim), dtype=torch.uint8, device=q.device)
     scale = 1.0 / math.sqrt(head_dim)
     with torch.cuda.device(q.device):
-        rc = lib.scree_attn_bwd(
+        rc = lib.scree_attn_bwd_gqa(
             do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
-            cu.data_ptr(), is64, batch, total, n_heads, head_dim, _lib.dtype_code(q.dtype),
+            cu.data_ptr(), is64, batch, total, n_heads, k.shape[1], head_dim, _lib.dtype_code(q.dtype),
             1 if causal else 0, scale, 0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
             ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device),
         )
@@ -189,7 +202,7 @@ def varlen_attention_fp32(q, k, v, cu_seqlens, causal: bool = False):
     """fp32 varlen attention forward on CUDA-core fp32 kernels (fp32-grade
     results); returns (out, lse).  The reference's Array-level op computes in the
     caller's dtype, fp32 included (scree/kernels/reference/varlen_attention.py:90-114)."""
-    assert q.shape == k.shape == v.shape, "q, k, v must have identical shape"
+    _check_qkv_shapes(q, k, v)
     assert q.is_cuda and q.dtype == torch.float32, "fp32 CUDA tensors expected"
     assert k.dtype == q.dtype and v.dtype == q.dtype, "q, k, v must share a dtype"
     total, n_heads, head_dim = q.shape
@@ -200,10 +213,10 @@ def varlen_attention_fp32(q, k, v, cu_seqlens, causal: bool = False):
         return out, lse
     q, k, v = (t if t.stride(2) == 1 else t.contiguous() for t in (q, k, v))
     with torch.cuda.device(q.device):
-        rc = _lib.load().scree_attn_fwd(
+        rc = _lib.load().scree_attn_fwd_gqa(
             q.data_ptr(), k.data_ptr(), v.data_ptr(),
             q.stride(0), q.stride(1), k.stride(0), k.stride(1), v.stride(0), v.stride(1),
-            cu.data_ptr(), is64, cu.numel() - 1, total, n_heads, head_dim, _lib.F32,
+            cu.data_ptr(), is64, cu.numel() - 1, total, n_heads, k.shape[1], head_dim, _lib.F32,
             1 if causal else 0, 1.0 / math.sqrt(head_dim), 0,
             out.data_ptr(), out.stride(0), out.stride(1), lse.data_ptr(), None, 0,
             _lib.stream_ptr(q.device),
@@ -224,9 +237,9 @@ def varlen_attention_fp32_backward(do, q, k, v, o, lse, cu_seqlens, causal: bool
     ws = torch.empty(lib.scree_attn_bwd_workspace_size(cu.numel() - 1, total, n_heads, head_dim),
                      dtype=torch.uint8, device=q.device)
     with torch.cuda.device(q.device):
-        rc = lib.scree_attn_bwd(
+        rc = lib.scree_attn_bwd_gqa(
             do.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.contiguous().data_ptr(),
-            cu.data_ptr(), is64, cu.numel() - 1, total, n_heads, head_dim, _lib.F32,
+            cu.data_ptr(), is64, cu.numel() - 1, total, n_heads, k.shape[1], head_dim, _lib.F32,
             1 if causal else 0, 1.0 / math.sqrt(head_dim), 0, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
             ws.data_ptr(), ws.numel(), _lib.stream_ptr(q.device),
         )
