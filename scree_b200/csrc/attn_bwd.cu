@@ -42,9 +42,7 @@ constexpr int BN = 128;  // keys per CTA
 // thread (65,536 / 512); the P/dS warpgroups grow to 152, warpgroup 2 shrinks to
 // 80 and warpgroup 3 to 120: 256 x 152 + 128 x 80 + 128 x 120 = 64,512 <= 65,536.
 constexpr int kThreads = 512;
-#ifndef SCREE_BWD_PINGPONG
-#define SCREE_BWD_PINGPONG 0  // D = 128 runs the two-tile kernel (attn_bwd_pp_kernel)
-#endif
+
 constexpr int kRegsSoftmax = 152, kRegsOther = 80, kRegsDq = 120;
 
 template <int D>
@@ -592,438 +590,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// ---------------------------------------------------------------------------
-// D = 128: two query tiles in flight ("ping-pong").
-//
-// The single-tile kernel above keeps one S^T / dP^T pair in TMEM, so every
-// tile's GEMMs wait on that tile's softmax work and the tensor pipe idles
-// while P and dS are formed.  Here query tiles of 64 rows alternate between two
-// TMEM slots X = i & 1, each holding S^T_X (64 columns) and dP^T_X (64
-// columns); dV and dK take the remaining 256.  While the P/dS warps work on
-// tile i, the tensor pipe runs tile i's dV / dK / dQ and tile i+1's S^T / dP^T.
-// Issue order of the MMA thread for tile i (slot X, the other slot Y):
-//   dV += P^T_i dO_i;  dP^T_{i+1} into Y (deferred until the dQ warps drained
-//   dQ_{i-1} from Y's dP^T columns);  dK += dS^T_i Q_i;  dQ^T_i = K^T dS^T_i
-//   over X's dP^T columns;  S^T_{i+2} into X.
-// TMEM: S^T_X [64X, 64X+64), dP^T_X / dQ^T_X [128+64X, 192+64X), dV [256,384),
-// dK [384,512).  Shared memory: K, V, a three-stage Q / dO ring, dS^T per slot,
-// the fp32 dQ staging tile of the bulk reduce-add, and a two-stage LSE / Delta
-// ring filled by two loader warps.
-struct PPCfg {
-  static constexpr int D = 128, BQP = 64;  // queries per tile
-  static constexpr int SWB = 128, CHUNK = 64, NCHUNK = 2;
-  static constexpr int QSTAGES = 3;
-  static constexpr int KV_BYTES = BN * D * 2;      // 32 KB
-  static constexpr int QT_BYTES = BQP * D * 2;     // 16 KB
-  static constexpr int DS_BYTES = BN * BQP * 2;    // 16 KB
-  static constexpr int DQ_BYTES = BQP * D * 4;     // 32 KB
-  static constexpr int OFF_K = 0;
-  static constexpr int OFF_V = OFF_K + KV_BYTES;
-  static constexpr int OFF_Q = OFF_V + KV_BYTES;
-  static constexpr int OFF_DO = OFF_Q + QSTAGES * QT_BYTES;
-  static constexpr int OFF_DS = OFF_DO + QSTAGES * QT_BYTES;  // [2]
-  static constexpr int OFF_DQ = OFF_DS + 2 * DS_BYTES;
-  static constexpr int OFF_LD = OFF_DQ + DQ_BYTES;            // [2][lse BQP | delta BQP]
-  static constexpr int OFF_BAR = OFF_LD + 2 * 2 * BQP * 4;
-  static constexpr int OFF_END = OFF_BAR + 512;
-  static constexpr int SMEM = OFF_END + 1024 <= 232448 ? OFF_END + 1024 : OFF_END;
-  static constexpr int COL_S = 0, COL_DP = 128, COL_DV = 256, COL_DK = 384;
-  static_assert(OFF_END <= 232448, "shared memory budget");
-};
-// Warp roles as in the single-tile kernel; registers: P/dS warpgroups 152, the
-// TMA / MMA / loader warpgroup 80, the dQ warpgroup 120:
-// 256 x 152 + 128 x 80 + 128 x 120 = 64,512 <= 65,536.
-constexpr int kPPRegsSoftmax = 152, kPPRegsOther = 80, kPPRegsDq = 120;
-
-template <typename T, bool CAUSAL>
-__global__ void __launch_bounds__(kThreads, 1)
-    attn_bwd_pp_kernel(const __grid_constant__ CUtensorMap tm_q,
-                       const __grid_constant__ CUtensorMap tm_k,
-                       const __grid_constant__ CUtensorMap tm_v,
-                       const __grid_constant__ CUtensorMap tm_do,
-                       const __grid_constant__ CUtensorMap tm_dq, const BwdParams p) {
-  using C = PPCfg;
-  constexpr int D = C::D, BQP = C::BQP;
-  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t ID_S = make_idesc_f16(BN, BQP, kBF16, false, false);
-  constexpr uint32_t ID_ACC = make_idesc_f16(BN, D, kBF16, false, true);
-  constexpr uint32_t ID_DQ = make_idesc_f16(D, BQP, kBF16, true, true);
-
-  const int64_t item = blockIdx.x;
-  if (item >= total_items(p.sched)) return;
-  if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
-  const WorkItem wi = decode_item(p.sched, p.B, p.Hkv, item);
-  const int h = wi.head;  // K / V head
-  const int64_t row0 = load_offset(p.offs, p.is64, wi.seq);
-  const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - row0);
-  const int k0 = wi.j * BN;
-  const int nq = (L + BQP - 1) / BQP;
-  const int i_first = CAUSAL ? k0 / BQP : 0;
-  const int n_it = nq - i_first;
-  const int n_all = n_it * p.G;  // tiles of all G query heads of this K / V head
-  auto q_tile = [&](int it_) { return i_first + it_ % n_it; };
-  auto q_head = [&](int it_) { return h * p.G + it_ / n_it; };
-
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~uintptr_t(1023));
-  {
-    uint32_t dyn;
-    asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
-    if ((uint32_t)(smem - smem_raw) + (uint32_t)C::OFF_END > dyn) {
-      if (threadIdx.x == 0) record_device_error(p.status, SCREE_DEVERR_BAD_INPUT, 92);
-      return;
-    }
-  }
-  const uint32_t sK = smem_u32(smem + C::OFF_K), sV = smem_u32(smem + C::OFF_V);
-  const uint32_t sQ = smem_u32(smem + C::OFF_Q), sDO = smem_u32(smem + C::OFF_DO);
-  const uint32_t sDS = smem_u32(smem + C::OFF_DS);
-  float* lds = reinterpret_cast<float*>(smem + C::OFF_LD);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* kv_full = bars;
-  uint64_t* q_full = kv_full + 1;     // [QSTAGES]
-  uint64_t* q_empty = q_full + 3;     // [QSTAGES]
-  uint64_t* s_full = q_empty + 3;     // [2] per slot
-  uint64_t* dp_full = s_full + 2;     // [2]
-  uint64_t* p_full = dp_full + 2;     // [2]
-  uint64_t* ds_full = p_full + 2;     // [2]
-  uint64_t* p_free = ds_full + 2;     // [2]
-  uint64_t* ds_free = p_free + 2;     // [2]
-  uint64_t* dq_full = ds_free + 2;    // [2]
-  uint64_t* dq_empty = dq_full + 2;   // [2]
-  uint64_t* ld_full = dq_empty + 2;   // [2]
-  uint64_t* ld_empty = ld_full + 2;   // [2]
-  uint64_t* acc_done = ld_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
-    for (int s = 0; s < C::QSTAGES; ++s) {
-      mbar_init(&q_full[s], 1);
-      mbar_init(&q_empty[s], 1);
-    }
-    for (int x = 0; x < 2; ++x) {
-      mbar_init(&s_full[x], 1);
-      mbar_init(&dp_full[x], 1);
-      mbar_init(&p_full[x], 256);
-      mbar_init(&ds_full[x], 256);
-      mbar_init(&p_free[x], 1);
-      mbar_init(&ds_free[x], 1);
-      mbar_init(&dq_full[x], 1);
-      mbar_init(&dq_empty[x], 128);
-      mbar_init(&ld_full[x], 64);
-      mbar_init(&ld_empty[x], 8);
-    }
-    mbar_init(acc_done, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 9) tmem_alloc<512>(tmem_slot);
-  if (warp == 8 && lane == 0) {
-    tma_prefetch_desc(&tm_q);
-    tma_prefetch_desc(&tm_k);
-    tma_prefetch_desc(&tm_v);
-    tma_prefetch_desc(&tm_do);
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 8) {
-    // ------------------------------------------------------------ TMA producer
-    regs_dec<kPPRegsOther>();
-    if (elect_one()) {
-      mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
-#pragma unroll
-      for (int c = 0; c < C::NCHUNK; ++c) {
-        tma_load_3d(smem + C::OFF_K + c * BN * C::SWB, &tm_k, kv_full, c * C::CHUNK, h,
-                    (int)row0 + k0);
-        tma_load_3d(smem + C::OFF_V + c * BN * C::SWB, &tm_v, kv_full, c * C::CHUNK, h,
-                    (int)row0 + k0);
-      }
-      for (int it = 0; it < n_all; ++it) {
-        const int st = it % C::QSTAGES;
-        if (it >= C::QSTAGES &&
-            !mbar_wait(&q_empty[st], ((it / C::QSTAGES) - 1) & 1, abort_flag, p.status, 51))
-          break;
-        const int qrow = (int)row0 + q_tile(it) * BQP, hq = q_head(it);
-        mbar_expect_tx(&q_full[st], 2 * C::QT_BYTES);
-#pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c) {
-          tma_load_3d(smem + C::OFF_Q + st * C::QT_BYTES + c * BQP * C::SWB, &tm_q, &q_full[st],
-                      c * C::CHUNK, hq, qrow);
-          tma_load_3d(smem + C::OFF_DO + st * C::QT_BYTES + c * BQP * C::SWB, &tm_do,
-                      &q_full[st], c * C::CHUNK, hq, qrow);
-        }
-      }
-    }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    regs_dec<kPPRegsOther>();
-    if (elect_one()) {
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 52);
-      auto qbuf = [&](int it_) { return sQ + (it_ % C::QSTAGES) * C::QT_BYTES; };
-      auto obuf = [&](int it_) { return sDO + (it_ % C::QSTAGES) * C::QT_BYTES; };
-      auto wait_q = [&](int it_) {
-        return mbar_wait(&q_full[it_ % C::QSTAGES], (it_ / C::QSTAGES) & 1, abort_flag, p.status, 53);
-      };
-      auto issue_s = [&](int it_) {  // S^T_X = K Q^T
-        const int x = it_ & 1;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16_ss(tmem + C::COL_S + x * BQP, kmaj<D>(sK, BN, kk), kmaj<D>(qbuf(it_), BQP, kk),
-                      ID_S, kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[x]);
-      };
-      auto issue_dp = [&](int it_) {  // dP^T_X = V dO^T
-        const int x = it_ & 1;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16_ss(tmem + C::COL_DP + x * BQP, kmaj<D>(sV, BN, kk), kmaj<D>(obuf(it_), BQP, kk),
-                      ID_S, kk > 0 ? 1u : 0u);
-        umma_commit(&dp_full[x]);
-      };
-      // Prologue: both slots' S^T and dP^T.
-      for (int it = 0; ok && it < 2 && it < n_all; ++it) {
-        if (!(ok = wait_q(it))) break;
-        tc_fence_after();
-        issue_s(it);
-        issue_dp(it);
-      }
-      for (int it = 0; ok && it < n_all; ++it) {
-        const int x = it & 1, y = x ^ 1;
-        const uint32_t par = (it >> 1) & 1;
-        // dV += P^T_it dO_it, A = P^T from TMEM
-        if (!(ok = mbar_wait(&p_full[x], par, abort_flag, p.status, 54))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQP / 16; ++kk)
-          umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + x * BQP + packed_col<BQP>(kk),
-                      mnmaj<D>(obuf(it), BQP, kk), ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&p_free[x]);
-        // dP^T_{it+1} into slot y once the dQ warps drained dQ_{it-1} from it
-        // (tiles 0 and 1 were issued in the prologue; Q / dO of it+1 are loaded:
-        // S^T_{it+1} was issued after waiting for them).
-        if (it >= 1 && it + 1 < n_all) {
-          if (!(ok = mbar_wait(&dq_empty[y], ((it - 1) >> 1) & 1, abort_flag, p.status, 55))) break;
-          tc_fence_after();
-          issue_dp(it + 1);
-        }
-        // dK += dS^T_it Q_it (A = dS^T from TMEM), then dQ^T_it = K^T dS^T_it over
-        // slot x's dP^T columns (dK has read dS^T from them: same issuer, in order).
-        if (!(ok = mbar_wait(&ds_full[x], par, abort_flag, p.status, 56))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQP / 16; ++kk)
-          umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + x * BQP + packed_col<BQP>(kk),
-                      mnmaj<D>(qbuf(it), BQP, kk), ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);
-        const uint32_t dsb = sDS + x * C::DS_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_f16_ss(tmem + C::COL_DP + x * BQP, mnmaj<D>(sK, BN, kk), pt_mnmaj(dsb, kk), ID_DQ,
-                      kk > 0 ? 1u : 0u);
-        umma_commit(&dq_full[x]);
-        umma_commit(&ds_free[x]);
-        umma_commit(&q_empty[it % C::QSTAGES]);
-        // S^T_{it+2} into slot x: P^T_it was read by dV_it (issued above).
-        if (it + 2 < n_all) {
-          if (!(ok = wait_q(it + 2))) break;
-          tc_fence_after();
-          issue_s(it + 2);
-        }
-      }
-      umma_commit(acc_done);
-    }
-  } else if (warp == 10 || warp == 11) {
-    // ------------------------------------------------------------ LSE / Delta loaders
-    regs_dec<kPPRegsOther>();
-    const int t64 = threadIdx.x - 320;
-    for (int it = 0; it < n_all; ++it) {
-      const int buf = it & 1;
-      if (it >= 2 && !mbar_wait(&ld_empty[buf], ((it >> 1) - 1) & 1, abort_flag, p.status, 57))
-        break;
-      const int q0 = q_tile(it) * BQP;
-      const int64_t hb = (int64_t)q_head(it) * p.T + row0;
-      float v[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {  // entries 2 t64, 2 t64 + 1 of [lse BQP | delta BQP]
-        const int idx = t64 * 2 + e;
-        const int q = q0 + (idx % BQP);
-        v[e] = q < L ? (idx < BQP ? p.lse2T[hb + q] : p.deltaT[hb + q]) : 0.f;
-      }
-      *reinterpret_cast<float2*>(lds + buf * 2 * BQP + t64 * 2) = make_float2(v[0], v[1]);
-      mbar_arrive(&ld_full[buf]);
-    }
-  } else if (warp < 8) {
-    // ------------------------------------------------------------ P^T / dS^T
-    regs_inc<kPPRegsSoftmax>();
-    constexpr int QH = BQP / 2;               // query columns per warp half
-    const int hf = warp >> 2;
-    const int kr = (warp & 3) * 32 + lane;    // key row == TMEM lane
-    const int kidx = k0 + kr;
-    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const bool key_ok = kidx < L;
-    const float sl2 = p.scale_log2;
-    bool ok = true;
-    for (int it = 0; it < n_all; ++it) {
-      const int x = it & 1;
-      const uint32_t par = (it >> 1) & 1;
-      const int q0 = q_tile(it) * BQP;
-      const int qh0 = q0 + hf * QH;
-      const float* lse_s = lds + x * 2 * BQP + hf * QH;
-      const float* del_s = lse_s + BQP;
-      const bool need_mask = (q0 + BQP > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
-      ok = mbar_wait(&ld_full[x], par, abort_flag, p.status, 58);
-      ok = ok && mbar_wait(&s_full[x], par, abort_flag, p.status, 59);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t col_s = lane_base + C::COL_S + x * BQP + hf * QH;
-      const uint32_t col_dp = lane_base + C::COL_DP + x * BQP + hf * QH;
-      float pr[QH];
-      tmem_ld32(col_s, *reinterpret_cast<float(*)[32]>(&pr[0]));
-      tmem_wait_ld();
-      uint32_t pk[QH / 2];
-#pragma unroll
-      for (int c4 = 0; c4 < QH / 4; ++c4) {
-        const float4 l4 = reinterpret_cast<const float4*>(lse_s)[c4];
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = c4 * 4 + e;
-          float xv = ex2_approx(fmaf(pr[c], sl2, -lv[e]));
-          if (need_mask) {
-            const int q = qh0 + c;
-            const bool valid = key_ok && q < L && (!CAUSAL || q >= kidx);
-            xv = valid ? xv : 0.f;
-          }
-          pr[c] = xv;
-        }
-        pk[c4 * 2] = Pk2b<T>::pack(pr[c4 * 4], pr[c4 * 4 + 1]);
-        pk[c4 * 2 + 1] = Pk2b<T>::pack(pr[c4 * 4 + 2], pr[c4 * 4 + 3]);
-      }
-      if (it >= 2) {  // dV_{it-2} read P^T_{it-2} from this slot
-        ok = mbar_wait(&p_free[x], ((it - 2) >> 1) & 1, abort_flag, p.status, 60);
-        if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      }
-      // P^T packed over the first half of this warp half's own columns.
-      tmem_st16u(col_s, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[x]);
-      // ---- dS^T = P^T (dP^T - Delta)
-      ok = mbar_wait(&dp_full[x], par, abort_flag, p.status, 61);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      tc_fence_after();
-      {
-        float dp[32];
-        tmem_ld32(col_dp, dp);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
-          const float4 d4 = reinterpret_cast<const float4*>(del_s)[e4];
-          pr[e4 * 4 + 0] *= (dp[e4 * 4 + 0] - d4.x);
-          pr[e4 * 4 + 1] *= (dp[e4 * 4 + 1] - d4.y);
-          pr[e4 * 4 + 2] *= (dp[e4 * 4 + 2] - d4.z);
-          pr[e4 * 4 + 3] *= (dp[e4 * 4 + 3] - d4.w);
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ld_empty[x]);  // this warp is done with LSE / Delta
-#pragma unroll
-      for (int c = 0; c < QH / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
-      if (it >= 2) {  // the dQ GEMM of tile it-2 read this slot's dS^T buffer
-        ok = mbar_wait(&ds_free[x], ((it - 2) >> 1) & 1, abort_flag, p.status, 62);
-        if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      }
-      tmem_st16u(col_dp, pk);
-      write_row_sw128<T, QH>(smem + C::OFF_DS + x * C::DS_BYTES, kr, pr, hf * (QH / 8));
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&ds_full[x]);
-    }
-    // ---- dK, dV epilogue: 32-column chunk c belongs to half c % 2
-    if (ok) {
-      ok = mbar_wait(acc_done, 0, abort_flag, p.status, 63);
-      ok = __all_sync(0xffffffff, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      T* dvrow = reinterpret_cast<T*>(p.dv) + ((row0 + kidx) * p.Hkv + h) * D;
-      T* dkrow = reinterpret_cast<T*>(p.dk) + ((row0 + kidx) * p.Hkv + h) * D;
-#pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int col = pass == 0 ? C::COL_DV : C::COL_DK;
-        const float mul = pass == 0 ? 1.f : p.scale;
-        T* dst = pass == 0 ? dvrow : dkrow;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          if ((c & 1) != hf) continue;
-          float v[32];
-          tmem_ld32(lane_base + col + c * 32, v);
-          tmem_wait_ld();
-          if (key_ok) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 w;
-              w.x = Pk2b<T>::pack(v[u * 8 + 0] * mul, v[u * 8 + 1] * mul);
-              w.y = Pk2b<T>::pack(v[u * 8 + 2] * mul, v[u * 8 + 3] * mul);
-              w.z = Pk2b<T>::pack(v[u * 8 + 4] * mul, v[u * 8 + 5] * mul);
-              w.w = Pk2b<T>::pack(v[u * 8 + 6] * mul, v[u * 8 + 7] * mul);
-              *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = w;
-            }
-          }
-        }
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ dQ warps 12-15
-    // Lane = feature d, column = query: drain dQ^T_it (64 columns) from slot x's
-    // dP^T columns, stage it as [64 q][D] fp32 and add it into dq_acc with one
-    // bulk tensor reduce.  Queries >= L carry exact zeros (their dS is 0).
-    regs_dec<kPPRegsDq>();
-    const int ln = threadIdx.x - 384;
-    const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
-    const float sc = p.scale;
-    float* sdq = reinterpret_cast<float*>(smem + C::OFF_DQ);
-    for (int it = 0; it < n_all; ++it) {
-      const int x = it & 1;
-      bool ok = mbar_wait(&dq_full[x], (it >> 1) & 1, abort_flag, p.status, 64);
-      if (!__all_sync(0xffffffff, ok)) break;
-      tc_fence_after();
-      float v[BQP];
-      tmem_ld32(lane_base + C::COL_DP + x * BQP, *reinterpret_cast<float(*)[32]>(&v[0]));
-      tmem_ld32(lane_base + C::COL_DP + x * BQP + 32, *reinterpret_cast<float(*)[32]>(&v[32]));
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&dq_empty[x]);
-      if (ln == 0 && it > 0) bulk_wait_read_all();
-      dq_group_sync();
-#pragma unroll
-      for (int c = 0; c < BQP; ++c) sdq[c * D + ln] = v[c] * sc;
-      fence_proxy_async_smem();
-      dq_group_sync();
-      if (ln == 0) {
-        tma_reduce_add_3d(&tm_dq, sdq, 0, q_head(it), (int)(row0 + q_tile(it) * BQP));
-        bulk_commit();
-      }
-    }
-    if (ln == 0) bulk_wait_all();  // shared memory must outlive the reduces
-  }
-
-  __syncwarp();
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 9) {
-    tc_fence_after();
-    tmem_dealloc<512>(tmem);
-  }
-}
-
 // Delta[h][t] = sum_d O[t,h,d] * dO[t,h,d] (fp32) and lse2T[h][t] = lse[t,h] * log2(e).
 // 8 threads per (t, h) row, 16-byte loads.
 template <typename T, int D>
@@ -1088,25 +654,6 @@ int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   }
   ProfScope prof(PROF_ATTN_BWD, s);
   kern<<<(unsigned)grid, kThreads, BwdCfg<D>::SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
-  SCREE_LAUNCH_CHECK();
-  return SCREE_OK;
-}
-
-template <typename T, bool CAUSAL>
-int launch_bwd_pp(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
-                  const CUtensorMap& tdo, const CUtensorMap& tdq, const BwdParams& p,
-                  int64_t grid, cudaStream_t s) {
-  auto kern = attn_bwd_pp_kernel<T, CAUSAL>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    SCREE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        PPCfg::SMEM));
-    attr_set[dev & 63] = true;
-  }
-  ProfScope prof(PROF_ATTN_BWD, s);
-  kern<<<(unsigned)grid, kThreads, PPCfg::SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
@@ -1180,12 +727,6 @@ int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v,
     set_last_error("attn_bwd: grid too large");
     return SCREE_ERR_INVALID;
   }
-#if SCREE_BWD_PINGPONG
-  if (D == 128) {
-    rc = causal ? launch_bwd_pp<T, true>(tq, tk, tv, tdo, tdq, p, grid, s)
-                : launch_bwd_pp<T, false>(tq, tk, tv, tdo, tdq, p, grid, s);
-  } else
-#endif
 #define SCREE_BWD_CASE(DD)                                                        \
   if (D == DD) {                                                                  \
     rc = causal ? launch_bwd<DD, T, true>(tq, tk, tv, tdo, tdq, p, grid, s)       \
