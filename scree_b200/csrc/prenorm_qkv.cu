@@ -1,0 +1,313 @@
+// prenorm_qkv.cu — RMSNorm fused into the QKV projection on sm_100a tensor cores.
+//
+// The caller side of the attention path in scree's examples
+// (examples/03_train_step.py:26-48, examples/02_no_pad_transformer.py:31-58):
+//   h = varlen_rmsnorm(x) * gamma;   qkv = h @ Wqkv   (then viewed as (T, 3, H, D))
+// RMSNorm is a per-row scale, so
+//   qkv[t, n] = rstd[t] * sum_c x[t, c] * (gamma[c] * Wqkv[c, n]),
+//   rstd[t]   = 1 / sqrt(mean_c x[t, c]^2 + eps).
+// One GEMM kernel computes it: the raw x tiles feed tcgen05.mma straight from
+// the TMA ring, the four epilogue warps read the same shared-memory x tiles to
+// accumulate each row's sum of squares while the tensor core works, and the
+// epilogue scales the fp32 accumulator row by rstd before the 16-bit store.  x
+// is read from HBM once and the normalised h never exists in memory.  gamma is
+// folded into the weight once per call (gamma[c] * Wqkv[c, :], a C x N pass);
+// with gamma = NULL the weight is used as is.
+//
+// Tile: 128 rows x BNT (= 256 or 128) columns per CTA, K in steps of 64
+// (128-byte swizzled rows), a 4-stage TMA ring.  Warp 0 issues TMA, warp 1 the
+// MMAs (M = 128, N = BNT, accumulator in TMEM), warps 2-5 are the row-statistics
+// and epilogue warps (warp w owns TMEM lanes 32 (w % 4) ..).  Stage s is free
+// again when the MMAs that read it completed (commit) and all 128 statistics
+// threads read their rows (mbarrier count 129).
+#include <algorithm>
+#include "attn_common.cuh"
+
+namespace scree {
+namespace {
+
+constexpr int QM = 128;         // rows per CTA
+constexpr int QK = 64;          // K per stage (one 128-byte swizzle row of 16-bit values)
+constexpr int QSTAGES = 4;
+constexpr int kQThreads = 192;  // TMA warp, MMA warp, 4 epilogue warps
+
+template <int BNT>
+struct QCfg {
+  static constexpr int A_BYTES = QM * QK * 2;    // 16 KB
+  static constexpr int B_BYTES = BNT * QK * 2;   // 32 KB at BNT = 256
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int OFF_BAR = QSTAGES * STAGE;
+  static constexpr int OFF_END = OFF_BAR + 128;
+  static constexpr int SMEM = OFF_END + 1024;
+};
+
+struct QParams {
+  int64_t T, N, C;
+  float eps;
+  void* y;           // (T, N) row-major, dtype
+  float* rstd;       // (T,) or nullptr
+  int* status;
+};
+
+template <typename T, int BNT>
+__global__ void __launch_bounds__(kQThreads, 1)
+    rmsnorm_qkv_kernel(const __grid_constant__ CUtensorMap tm_x,
+                       const __grid_constant__ CUtensorMap tm_w, const QParams p) {
+  using Cf = QCfg<BNT>;
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  // A = x tile (K-major), B = weight tile [K rows][N] (N contiguous: MN-major).
+  constexpr uint32_t IDESC = make_idesc_f16(QM, BNT, kBF16, false, true);
+  const int m0 = blockIdx.x * QM;
+  const int n0 = blockIdx.y * BNT;
+  const int nk = (int)(p.C / QK);
+  if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cf::OFF_BAR);
+  uint64_t* full = bars;                 // [QSTAGES]
+  uint64_t* empty = full + QSTAGES;      // [QSTAGES]
+  uint64_t* acc_full = empty + QSTAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < QSTAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1 + 128);  // MMA commit + the 128 statistics threads
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc<BNT>(tmem_slot);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA
+    if (elect_one()) {
+      for (int kt = 0; kt < nk; ++kt) {
+        const int s = kt % QSTAGES;
+        if (kt >= QSTAGES &&
+            !mbar_wait(&empty[s], ((kt / QSTAGES) - 1) & 1, abort_flag, p.status, 70))
+          break;
+        uint8_t* st = smem + s * Cf::STAGE;
+        mbar_expect_tx(&full[s], Cf::STAGE);
+        tma_load_2d(st, &tm_x, &full[s], kt * QK, m0);
+#pragma unroll
+        for (int j = 0; j < BNT / 64; ++j)  // 64-column chunks of [QK rows][64 N]
+          tma_load_2d(st + Cf::A_BYTES + j * QK * 128, &tm_w, &full[s], n0 + j * 64, kt * QK);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA
+    if (elect_one()) {
+      bool ok = true;
+      for (int kt = 0; ok && kt < nk; ++kt) {
+        const int s = kt % QSTAGES;
+        if (!(ok = mbar_wait(&full[s], (kt / QSTAGES) & 1, abort_flag, p.status, 71))) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(smem + s * Cf::STAGE);
+        const uint32_t b = a + Cf::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < QK / 16; ++kk)
+          umma_f16_ss(tmem, make_sdesc(a + kk * 32, 16, 1024, SW_128B),
+                      make_sdesc(b + kk * 16 * 128, QK * 128, 1024, SW_128B), IDESC,
+                      (kt > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      umma_commit(acc_full);
+    }
+  } else {
+    // ------------------------------------------------------------ statistics + epilogue
+    const int q = warp & 3;            // TMEM lane quarter of this warp
+    const int r = q * 32 + lane;       // row within the tile == TMEM lane
+    float ss = 0.f;
+    bool ok = true;
+    for (int kt = 0; kt < nk; ++kt) {
+      const int s = kt % QSTAGES;
+      ok = mbar_wait(&full[s], (kt / QSTAGES) & 1, abort_flag, p.status, 72);
+      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+      const uint8_t* row = smem + s * Cf::STAGE + r * 128;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // 16-byte chunks, 128B-swizzled by row
+        const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ (r & 7)) << 4));
+        const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const float f = Cvt<T>::to_f(e[u]);
+          ss = fmaf(f, f, ss);
+        }
+      }
+      // These generic-proxy reads must be ordered before the TMA (async proxy)
+      // refill of the stage that this arrival allows.
+      fence_proxy_async_smem();
+      mbar_arrive(&empty[s]);
+    }
+    if (ok) {
+      ok = mbar_wait(acc_full, 0, abort_flag, p.status, 73);
+      ok = __all_sync(0xffffffff, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const float rs = rsqrtf(ss / (float)p.C + p.eps);
+      const int64_t t = (int64_t)m0 + r;
+      const bool row_ok = t < p.T;
+      if (row_ok && blockIdx.y == 0 && p.rstd != nullptr) p.rstd[t] = rs;
+      T* yrow = reinterpret_cast<T*>(p.y) + t * p.N + n0;
+      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BNT / 32; ++c) {
+        float v[32];
+        tmem_ld32_sync(lane_base + c * 32, v);
+        if (row_ok) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = v[u * 8 + e] * rs;
+            alignas(16) T pk[8];
+            cvt_from_f<T, 8>(o, pk);
+            *reinterpret_cast<uint4*>(yrow + c * 32 + u * 8) = *reinterpret_cast<const uint4*>(pk);
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<BNT>(tmem);
+  }
+}
+
+// W'[c][n] = gamma[c] * W[c][n], rounded to the weight's dtype.
+template <typename T, typename G>
+__global__ void fold_gamma_kernel(const T* __restrict__ w, const G* __restrict__ gamma,
+                                  T* __restrict__ out, int64_t C, int64_t N) {
+  const int64_t n8 = N / 8;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < C * n8;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = i / n8;
+    const float g = Cvt<G>::to_f(gamma[c]);
+    uint4 raw = reinterpret_cast<const uint4*>(w)[i];
+    const T* e = reinterpret_cast<const T*>(&raw);
+    float f[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) f[u] = Cvt<T>::to_f(e[u]) * g;
+    alignas(16) T pk[8];
+    cvt_from_f<T, 8>(f, pk);
+    reinterpret_cast<uint4*>(out)[i] = *reinterpret_cast<const uint4*>(pk);
+  }
+}
+
+int make_2d_map(CUtensorMap* map, const void* base, int64_t inner, int64_t outer,
+                int64_t row_stride_elems, int box_inner, int box_outer, bool bf16) {
+  EncodeTiledFn enc = get_encode_tiled();
+  if (!enc) {
+    set_last_error("cuTensorMapEncodeTiled is unavailable from the driver");
+    return SCREE_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                   const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("cuTensorMapEncodeTiled (2-D) failed (CUresult %d)", (int)r);
+    return SCREE_ERR_CUDA;
+  }
+  return SCREE_OK;
+}
+
+template <typename T, int BNT>
+int launch_qkv(const CUtensorMap& tx, const CUtensorMap& tw, const QParams& p, cudaStream_t s) {
+  auto kern = rmsnorm_qkv_kernel<T, BNT>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    SCREE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        QCfg<BNT>::SMEM));
+    attr_set[dev & 63] = true;
+  }
+  const dim3 grid((unsigned)((p.T + QM - 1) / QM), (unsigned)(p.N / BNT));
+  kern<<<grid, kQThreads, QCfg<BNT>::SMEM, s>>>(tx, tw, p);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+}  // namespace
+}  // namespace scree
+
+using namespace scree;
+
+extern "C" size_t scree_rmsnorm_qkv_workspace_size(int64_t C, int64_t N) {
+  return (size_t)C * N * 2;
+}
+
+extern "C" int scree_rmsnorm_qkv_fwd(const void* x, int64_t x_row_stride, const void* gamma,
+                                     int g_dtype, const void* weight, void* y, float* rstd,
+                                     int64_t T, int64_t C, int64_t N, int dtype, float eps,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  SCREE_CHECK_ARG(T >= 0 && C >= 1 && N >= 1, "rmsnorm_qkv: bad sizes");
+  SCREE_CHECK_ARG(dtype == SCREE_F16 || dtype == SCREE_BF16, "rmsnorm_qkv: fp16 or bf16 only");
+  if (C % QK != 0 || N % 128 != 0) {
+    set_last_error("rmsnorm_qkv: C must be a multiple of 64 and N of 128 (C=%lld N=%lld)",
+                   (long long)C, (long long)N);
+    return SCREE_ERR_UNSUPPORTED;
+  }
+  SCREE_CHECK_ARG(T < (1ll << 31) && C < (1ll << 31) && N < (1ll << 31), "rmsnorm_qkv: too large");
+  if (T == 0) return SCREE_OK;
+  SCREE_CHECK_ARG(x && weight && y, "rmsnorm_qkv: null pointer");
+  SCREE_CHECK_ARG(((uintptr_t)x % 16) == 0 && (x_row_stride % 8) == 0 && ((uintptr_t)weight % 16) == 0 &&
+                      ((uintptr_t)y % 16) == 0,
+                  "rmsnorm_qkv: 16-byte aligned tensors and row strides required");
+  SCREE_BIND_DEVICE(stream, x);
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool bf16 = dtype == SCREE_BF16;
+  const void* w = weight;
+  if (gamma != nullptr) {  // fold gamma into the weight rows once
+    SCREE_CHECK_ARG(workspace && workspace_bytes >= (size_t)C * N * 2,
+                    "rmsnorm_qkv: workspace too small");
+    SCREE_CHECK_ARG(g_dtype == SCREE_F16 || g_dtype == SCREE_BF16 || g_dtype == SCREE_F32,
+                    "rmsnorm_qkv: gamma dtype");
+    const int64_t n = C * N / 8;
+    const unsigned grid = (unsigned)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 8);
+#define SCREE_FOLD(TT)                                                                         \
+  switch (g_dtype) {                                                                           \
+    case SCREE_F32: fold_gamma_kernel<TT, float><<<grid, 256, 0, s>>>((const TT*)weight, (const float*)gamma, (TT*)workspace, C, N); break; \
+    case SCREE_BF16: fold_gamma_kernel<TT, __nv_bfloat16><<<grid, 256, 0, s>>>((const TT*)weight, (const __nv_bfloat16*)gamma, (TT*)workspace, C, N); break; \
+    default: fold_gamma_kernel<TT, __half><<<grid, 256, 0, s>>>((const TT*)weight, (const __half*)gamma, (TT*)workspace, C, N); break; \
+  }
+    if (bf16) { SCREE_FOLD(__nv_bfloat16) } else { SCREE_FOLD(__half) }
+#undef SCREE_FOLD
+    SCREE_LAUNCH_CHECK();
+    w = workspace;
+  }
+  CUtensorMap tx, tw;
+  int rc;
+  if ((rc = make_2d_map(&tx, x, C, T, x_row_stride, QK, QM, bf16))) return rc;
+  const int bnt = (N % 256 == 0) ? 256 : 128;
+  if ((rc = make_2d_map(&tw, w, N, C, N, 64, QK, bf16))) return rc;
+  QParams p{T, N, C, eps, y, rstd, device_status_ptr()};
+  ProfScope prof(PROF_NORM_FWD, s);
+  if (bf16)
+    return bnt == 256 ? launch_qkv<__nv_bfloat16, 256>(tx, tw, p, s)
+                      : launch_qkv<__nv_bfloat16, 128>(tx, tw, p, s);
+  return bnt == 256 ? launch_qkv<__half, 256>(tx, tw, p, s) : launch_qkv<__half, 128>(tx, tw, p, s);
+}

@@ -37,6 +37,8 @@ __all__ = [
     "varlen_attention_fp32",
     "varlen_attention_fp32_backward",
     "varlen_attention_fp32_autograd",
+    "rmsnorm_qkv",
+    "rmsnorm_qkv_autograd",
 ]
 
 
@@ -471,3 +473,67 @@ def varlen_softmax_packed(values, offsets):
     assert values.is_cuda, "varlen_softmax requires CUDA tensors"
     assert values.dtype in (torch.float16, torch.bfloat16, torch.float32), "fp16, bf16 or fp32 only"
     return _VarlenSoftmax.apply(values, offsets)
+
+
+# --------------------------------------------------------------------------- fused pre-norm QKV
+
+
+def rmsnorm_qkv(x, gamma, weight, eps: float = 1e-6, want_rstd: bool = False):
+    """``(rmsnorm(x) * gamma) @ weight`` in one tcgen05 GEMM with the RMSNorm fused
+    into it (the caller-side sequence of scree/examples/03_train_step.py:36-41).
+
+    x: (T, C) fp16 / bf16 CUDA tensor (any row stride that is a multiple of 8);
+    gamma: (C,) or None; weight: (C, N) in x's dtype, N a multiple of 128 and C of
+    64.  Returns y (T, N) in x's dtype (view it as (T, 3, H, D) for attention),
+    and rstd (T,) fp32 when ``want_rstd``."""
+    assert x.is_cuda and x.ndim == 2 and x.dtype in (torch.float16, torch.bfloat16)
+    assert weight.ndim == 2 and weight.shape[0] == x.shape[1] and weight.dtype == x.dtype
+    T, C = x.shape
+    N = weight.shape[1]
+    if x.stride(1) != 1 or x.stride(0) % 8 != 0 or x.data_ptr() % 16 != 0:
+        x = x.contiguous()
+    weight = weight.contiguous()
+    y = torch.empty((T, N), dtype=x.dtype, device=x.device)
+    rstd = torch.empty(T, dtype=torch.float32, device=x.device) if want_rstd else None
+    lib = _lib.load()
+    ws = None
+    if gamma is not None:
+        assert gamma.shape == (C,) and gamma.device == x.device
+        gamma = gamma.contiguous()
+        ws = torch.empty(lib.scree_rmsnorm_qkv_workspace_size(C, N), dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = lib.scree_rmsnorm_qkv_fwd(
+            x.data_ptr(), x.stride(0), _ptr(gamma), _wcode(gamma, x), weight.data_ptr(), y.data_ptr(),
+            _ptr(rstd), T, C, N, _lib.dtype_code(x.dtype), float(eps), _ptr(ws),
+            ws.numel() if ws is not None else 0, _lib.stream_ptr(x.device),
+        )
+    _lib.check(rc, "rmsnorm_qkv")
+    return (y, rstd) if want_rstd else y
+
+
+class _RMSNormQKV(torch.autograd.Function):
+    """Forward: the fused kernel.  Backward: h = rmsnorm(x) * gamma recomputed by
+    the RMSNorm kernel, dH = dY W^T and dW = h^T dY as library GEMMs, then dx and
+    dgamma from the RMSNorm backward kernel."""
+
+    @staticmethod
+    def forward(ctx, x, gamma, weight, eps):
+        y, rstd = rmsnorm_qkv(x, gamma, weight, eps, want_rstd=True)
+        ctx.save_for_backward(x, gamma, weight, rstd)
+        ctx.eps = eps
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, gamma, weight, rstd = ctx.saved_tensors
+        h = varlen_rmsnorm_triton(x, gamma, ctx.eps)
+        dy = dy.contiguous()
+        dh = dy @ weight.t()
+        dw = h.t() @ dy if ctx.needs_input_grad[2] else None
+        dx, dg = varlen_rmsnorm_backward(dh, x, gamma, rstd)
+        return dx, (dg if gamma is not None and ctx.needs_input_grad[1] else None), dw, None
+
+
+def rmsnorm_qkv_autograd(x, gamma, weight, eps: float = 1e-6):
+    """Differentiable rmsnorm_qkv."""
+    return _RMSNormQKV.apply(x, gamma, weight, eps)
