@@ -368,6 +368,42 @@ def measure_norms(steps, warmup, with_cpu=True):
     return res, cpu, hbm, kind, T
 
 
+def measure_prenorm_qkv(steps, warmup):
+    """Fused RMSNorm -> QKV projection on cfg3's rows (T = 19,794, hidden 4096, bf16)
+    with a (4096, 3 x 4096) weight: 2 T C N FLOPs per call, timed per launch with
+    CUDA events (L2 flushed before each) against the burst bf16 GEMM peak."""
+    import torch
+
+    from scree_b200 import _lib, workloads
+    from scree_b200.kernels import native
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    T, C, N = sum(workloads.cfg3_lengths()), 4096, 3 * 4096
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn((T, C), device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn((C, N), device=dev, generator=g) / 64).to(torch.bfloat16)
+    gamma = 1 + 0.02 * torch.randn(C, device=dev, generator=g)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(max(3, warmup)):
+        native.rmsnorm_qkv(x, gamma, w, 1e-6)
+    times = []
+    _lib.profile_read(_lib.PROF_NORM_FWD)
+    _lib.profile_enable(True)
+    for _ in range(steps):
+        flush.fill_(1)
+        native.rmsnorm_qkv(x, gamma, w, 1e-6)
+        torch.cuda.synchronize()
+        times.append(_lib.profile_read(_lib.PROF_NORM_FWD)[0])
+    _lib.profile_enable(False)
+    ms = statistics.median(times)
+    peaks, kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    tf = 2.0 * T * C * N / (ms / 1e3) / 1e12
+    return {"workload": f"x ({T}, {C}) bf16 (cfg3 rows), Wqkv ({C}, {N}), gamma fp32; y = rmsnorm(x) * gamma @ Wqkv",
+            "ms": ms, "tflops": tf, "frac": tf / peak, "peak_tflops": peak,
+            "peak_source": f"{kind} bf16_tflops (burst)", "note": "GEMM kernel time; the gamma-folding pass over the weight (C x N) is a separate launch"}
+
+
 def run_norm_suite(args):
     import torch
 
@@ -450,11 +486,14 @@ def main():
     from scree_b200 import shard
 
     if args.shard == "heads":
-        plan = shard.plan_units(lengths, world, H)
+        # (sequence, head group) units, split as finely as the balance needs;
+        # every (sequence, head) of a rank's units is laid out as its own packed
+        # single-head sequence, so the rank runs ONE attention call (H = 1) over
+        # all of them whatever their head counts (heads are independent).
+        plan = shard.plan_units(lengths, world, H, max_groups=H)
         if world > 1:
             plan = shard.broadcast_plan(plan)
-        groups = [(hs, [lengths[u.seq] for u in us])
-                  for hs, us in sorted(shard.units_by_heads(plan[rank]).items(), reverse=True)]
+        groups = [(1, [lengths[u.seq] for u in plan[rank] for _ in range(u.heads)])]
         args.no_e2e = True  # the end-to-end path is measured on whole sequences
         args.no_gather = True
     else:
@@ -664,6 +703,7 @@ def main():
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
 
     norms = None
+    prenorm_qkv = None
     if world == 1 and not args.no_norms:
         nres, ncpu, hbm, nkind, nT = measure_norms(max(10, min(args.steps, 30)), args.warmup, not args.no_cpu_baseline)
         norms = {
@@ -674,6 +714,9 @@ def main():
                          "algorithmic_bytes": v_["algorithmic_bytes"]} for k_, v_ in nres.items()},
             "cpu_baseline": ncpu,
         }
+        prenorm_qkv = measure_prenorm_qkv(max(10, min(args.steps, 30)), args.warmup)
+    else:
+        prenorm_qkv = None
 
     if rank == 0:
         line = {
@@ -714,6 +757,7 @@ def main():
             "compute_only_ms": ms_step,
             "with_gather": with_gather,
             "norms": norms,
+            "prenorm_qkv": prenorm_qkv,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": int(total_launch),
