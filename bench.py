@@ -573,14 +573,14 @@ def main():
         offs_g = np.concatenate([[0], np.cumsum(lengths)])
         mine = shard.local_shard(offs_g, plan, rank)
         T_all = int(offs_g[-1])
+        gplan = shard.GatherPlan(plan, offs_g, rank, dev)
 
         def step_gather():
             for t in (q, k, v):
                 t.grad = None
             out = varlen_attention_triton_autograd(q, k, v, cu, causal=causal)
             out.backward(do)
-            for t in (out.detach(), q.grad, k.grad, v.grad):
-                shard.gather_to_rank0(t, mine, T_all, plan=plan, global_offsets=offs_g)
+            gplan.run([out.detach(), q.grad, k.grad, v.grad])
 
         for _ in range(2):
             step_gather()
@@ -596,7 +596,7 @@ def main():
             "steps": g_steps,
             "value": float(sum(lengths)) / (float(gm[0]) / 1e3),
             "unit": "tokens/s",
-            "collective": "NCCL send/recv of every rank's O, dQ, dK, dV rows to rank 0 (batched P2P over NVLink) after each step's backward",
+            "collective": "NCCL send/recv to rank 0 of every rank's O, dQ, dK, dV rows, one message per sequence and tensor straight into rank 0's global-order outputs, one batch per step (NVLink), after each step's backward",
             "bytes_into_rank0_per_step": int(recv_bytes),
         }
 

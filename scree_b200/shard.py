@@ -163,6 +163,64 @@ def gather_to_rank0(local_values, shard: LocalShard, total_rows: int, group=None
     return out
 
 
+class GatherPlan:
+    """Precomputed exchange of per-rank outputs to rank 0 for a whole-sequence
+    plan: every sequence's rows travel as one contiguous message, straight into
+    its slice of rank 0's global-order output (no staging buffer, no scatter of
+    received rows), and all tensors of a step go in one batch of NCCL
+    send/recv operations.  Rank 0's own rows are placed with one index copy."""
+
+    def __init__(self, plan: List[List[int]], global_offsets, rank: int, device, group=None):
+        import torch
+
+        self.group = group
+        self.rank = rank
+        self.go = np.asarray(global_offsets, dtype=np.int64)
+        self.total = int(self.go[-1])
+        self.world = len(plan)
+        # (peer rank, local row range, global row range) per sequence
+        self.msgs = []
+        for r, part in enumerate(plan):
+            lo = 0
+            for i in sorted(part):
+                n = int(self.go[i + 1] - self.go[i])
+                if n and r != 0:
+                    self.msgs.append((r, lo, lo + n, int(self.go[i]), int(self.go[i + 1])))
+                lo += n
+        self.own_rows = torch.as_tensor(local_shard(self.go, plan, 0).rows, device=device)
+
+    def _peer(self, r):
+        import torch.distributed as dist
+
+        return dist.get_global_rank(self.group, r) if self.group is not None else r
+
+    def run(self, tensors):
+        """All ranks pass their local (T_r, ...) tensors; rank 0 gets the global
+        (T, ...) tensors back, other ranks None."""
+        import torch
+        import torch.distributed as dist
+
+        ops, outs = [], None
+        if self.rank == 0:
+            outs = [torch.empty((self.total, *t.shape[1:]), dtype=t.dtype, device=t.device) for t in tensors]
+            for r, l0, l1, g0, g1 in self.msgs:
+                for o in outs:
+                    ops.append(dist.P2POp(dist.irecv, o[g0:g1], self._peer(r), self.group))
+        else:
+            srcs = [t.contiguous() for t in tensors]
+            for r, l0, l1, g0, g1 in self.msgs:
+                if r == self.rank:
+                    for t in srcs:
+                        ops.append(dist.P2POp(dist.isend, t[l0:l1], self._peer(0), self.group))
+        reqs = dist.batch_isend_irecv(ops) if ops else []
+        if self.rank == 0 and self.own_rows.numel():
+            for o, t in zip(outs, tensors):
+                o.index_copy_(0, self.own_rows, t)
+        for q in reqs:
+            q.wait()
+        return outs
+
+
 @dataclass(frozen=True)
 class Unit:
     """Attention work on heads [h0, h1) of one sequence."""

@@ -57,6 +57,12 @@ def _worker(rank, world, port, mode, q):
             return
         if mode == "ok_plan":  # row lists derived from the plan: only values are sent
             out = shard.gather_to_rank0(vals, mine, int(offs[-1]), plan=plan, global_offsets=offs)
+        elif mode == "gplan":  # one message per sequence into rank 0's output slices
+            outs = shard.GatherPlan(plan, offs, rank, torch.device("cpu")).run([vals, vals * 3])
+            out = None
+            if rank == 0:
+                assert torch.equal(outs[1], outs[0] * 3)
+                out = outs[0]
         else:
             out = shard.gather_to_rank0(vals, mine, int(offs[-1]))
         if rank == 0:
@@ -133,7 +139,7 @@ def test_two_ranks_gather_global_order():
     assert res[0][2] is True and res[1][2] is True
 
 
-@pytest.mark.parametrize("mode", ["ok", "ok_plan"])
+@pytest.mark.parametrize("mode", ["ok", "ok_plan", "gplan"])
 def test_three_ranks_gather_point_to_point(mode):
     """Ranks 1 and 2 send to rank 0 only; rank 0 rebuilds global order, with the
     row lists sent or derived from the plan."""
