@@ -47,10 +47,11 @@ constexpr int ROWS = 2 * BM; // query rows per CTA (tiles A and B)
 constexpr int BN = 128;      // keys per K/V tile
 // 8 softmax warps (warpgroups 0, 1), then warpgroup 2: TMA warp, MMA warp and two
 // idle warps.  Launched at 168 registers per thread (65,536 / 384); the
-// softmax warpgroups grow to 224 and warpgroup 2 shrinks to 56:
-// 256 x 224 + 128 x 56 = 64,512 = 384 x 168.
+// softmax warpgroups grow to 208 and warpgroup 2 shrinks to 88:
+// 256 x 208 + 128 x 88 = 64,512 = 384 x 168.  (224 / 56 left the MMA and TMA
+// warps spilling and measured 3% slower.)
 constexpr int kThreads = 384;
-constexpr int kRegsSoftmax = 224, kRegsOther = 56;
+constexpr int kRegsSoftmax = 208, kRegsOther = 88;
 // P_X(j) is handed to the MMA warp in kPParts parts (of BN / kPParts keys);
 // 2 parts measured 1.5% faster than 1 and 4% faster than 4 at cfg4.
 #ifndef SCREE_P_PARTS
