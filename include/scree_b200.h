@@ -117,6 +117,23 @@ int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, int64_t q_ro
                        int64_t o_row_stride, int64_t o_head_stride, float* lse, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* KV-cache attention forward (no reference counterpart; docs/kernels.md:178
+ * lists KV-cache support as planned): queries and keys have offsets of their
+ * own.  q / o: (Tq, H, D) with offsets_q; k / v: (Tk, H_kv, D) with offsets_k;
+ * both arrays hold B + 1 entries of the same integer type.  Causal masking is
+ * aligned at the end of each sequence: query i of a sequence with Lq queries
+ * and Lk keys sees keys j <= i + (Lk - Lq) (decode and chunked prefill against
+ * a cache that already holds the earlier tokens).  A query with no key gets
+ * O = 0 and LSE = -inf.  Workspace: scree_attn_fwd_workspace_size(B, Tq, H, D).
+ * Both offsets arrays are validated on the device. */
+int scree_attn_fwd_kv(const void* q, const void* k, const void* v, int64_t q_row_stride,
+                      int64_t q_head_stride, int64_t k_row_stride, int64_t k_head_stride,
+                      int64_t v_row_stride, int64_t v_head_stride, const void* offsets_q,
+                      const void* offsets_k, int offs_is_i64, int64_t B, int64_t Tq, int64_t Tk,
+                      int64_t H, int64_t H_kv, int D, int dtype, int causal, float scale, void* o,
+                      int64_t o_row_stride, int64_t o_head_stride, float* lse, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of scree_attn_fwd (no counterpart in the reference).
  * For callers that cannot allocate device memory when they run attention (an
  * engine with a fixed pre-planned memory arena, or a binding that only holds
@@ -255,6 +272,17 @@ int scree_to_padded_ex(const void* values, const void* offsets, int offs_is_i64,
                        int64_t max_len, int64_t row_bytes, int64_t elem_bytes,
                        const void* fill_pattern_host, int side_left, void* padded, void* mask,
                        int mask_elem_bytes, void* stream);
+
+/* KV-cache append (no reference counterpart; docs/kernels.md:178): out holds,
+ * for each sequence b, its Tc-buffer rows cache[cache_offsets[b] ..
+ * cache_offsets[b+1]) followed by its new rows fresh[fresh_offsets[b] ..
+ * fresh_offsets[b+1]); out_offsets (B+1, int64) = cache_offsets + fresh_offsets
+ * is written on the device.  out: (Tc + Tn, ...) rows of row_bytes bytes.
+ * max_rows: the longest output sequence (sizes the grid; <= 0 for unknown). */
+int scree_kv_append(const void* cache, const void* cache_offsets, const void* fresh,
+                    const void* fresh_offsets, int offs_is_i64, int64_t B, int64_t Tc, int64_t Tn,
+                    int64_t max_rows, int64_t row_bytes, void* out, int64_t* out_offsets,
+                    void* stream);
 
 /* from_padded, step 1: per-row lengths = mask.sum(1) and int32 offsets (B+1,).
  * Replaces: scree/_core.py:253-301 from_padded (torch branch :260-267), which

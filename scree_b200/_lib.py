@@ -52,6 +52,11 @@ _SIGNATURES = {
         _I,
         [_P, _P, _P, _P, _P, _P, _P, _I, _L, _L, _L, _L, _I, _I, _I, _F, _L, _P, _P, _P, _P, _S, _P],
     ),
+    "scree_attn_fwd_kv": (
+        _I,
+        [_P, _P, _P, _L, _L, _L, _L, _L, _L, _P, _P, _I, _L, _L, _L, _L, _L, _I, _I, _I, _F, _P, _L, _L, _P, _P, _S, _P],
+    ),
+    "scree_kv_append": (_I, [_P, _P, _P, _P, _I, _L, _L, _L, _L, _L, _P, _P, _P]),
     "scree_attn_fwd_noalloc": (
         _I,
         [_P, _P, _P, _L, _L, _L, _L, _L, _L, _P, _I, _L, _L, _L, _I, _I, _I, _F, _L, _P, _L, _L, _P, _P],

@@ -126,13 +126,16 @@ extern "C" int scree_validate_offsets(const void* offsets, int offs_is_i64, int6
                   (long long)T);
   SCREE_CHECK_ARG(offsets != nullptr, "validate_offsets: null offsets");
   SCREE_BIND_DEVICE(stream, offsets);
-  validate_offsets_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(offsets, offs_is_i64, B, T,
-                                                                 device_status_ptr());
-  SCREE_LAUNCH_CHECK();
-  return SCREE_OK;
+  return launch_validate_offsets(offsets, offs_is_i64, B, T, (cudaStream_t)stream);
 }
 
 namespace scree {
+
+int launch_validate_offsets(const void* offs, int is64, int64_t B, int64_t T, cudaStream_t stream) {
+  validate_offsets_kernel<<<1, 1024, 0, stream>>>(offs, is64, B, T, device_status_ptr());
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
 
 EncodeTiledFn get_encode_tiled() {
   static EncodeTiledFn fn = nullptr;

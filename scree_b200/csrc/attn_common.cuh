@@ -40,6 +40,9 @@ constexpr int kSiteBadOffsets = 40;
 // SCREE_DEVERR_BAD_INPUT status.
 int launch_build_schedule(const void* offs, int is64, int64_t B, int64_t T, int outer, int H,
                           void* ws, cudaStream_t stream);
+// The offsets check alone (same status on failure); kernels that later read the
+// status word at CTA start then do no work.
+int launch_validate_offsets(const void* offs, int is64, int64_t B, int64_t T, cudaStream_t stream);
 
 // Device side: item -> (seq, head, j) with j the rank of the tile within its
 // (seq, head) group (0 = first scheduled).

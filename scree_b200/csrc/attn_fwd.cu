@@ -92,6 +92,7 @@ struct FwdParams {
   int T;
   float scale_log2;
   const void* sched;  // schedule (attn_common.cuh)
+  const void* offs_k; // key / value offsets when they differ from the query offsets, else null
   int64_t B;
   int* status;  // device status word
   void* o;
@@ -148,14 +149,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const WorkItem wi = decode_item(p.sched, p.B, p.H, item);
   const int h = wi.head;
   const int64_t seq_start = load_offset(p.offs, p.is64, wi.seq);
-  const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - seq_start);
+  const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - seq_start);  // query rows
+  // Keys: the same rows, or (KV-cache attention) a sequence of its own; causal
+  // masking is then aligned at the end: query i sees keys <= i + (Lk - L).
+  int64_t kv_start = seq_start;
+  int Lk = L;
+  if (p.offs_k != nullptr) {
+    kv_start = load_offset(p.offs_k, p.is64, wi.seq);
+    Lk = (int)(load_offset(p.offs_k, p.is64, wi.seq + 1) - kv_start);
+  }
+  const int cdelta = Lk - L;
   // Causal: heaviest (last) 256-row block first within each (sequence, head).
   const int q0 = (CAUSAL ? (wi.ntiles - 1 - wi.j) : wi.j) * ROWS;
-  const int nk_all = (L + BN - 1) / BN;
+  const int nk_all = (Lk + BN - 1) / BN;
   // Key tiles each query tile needs (tile B may not exist at a sequence's end).
-  const int nA = CAUSAL ? min(nk_all, (q0 + BM - 1) / BN + 1) : nk_all;
+  auto tiles_upto = [&](int last_q) {
+    const int last_k = last_q + cdelta;
+    return last_k < 0 ? 0 : min(nk_all, last_k / BN + 1);
+  };
+  const int nA = CAUSAL ? tiles_upto(q0 + BM - 1) : nk_all;
   const bool hasB = q0 + BM < L;
-  const int nB = !hasB ? 0 : (CAUSAL ? min(nk_all, (q0 + 2 * BM - 1) / BN + 1) : nk_all);
+  const int nB = !hasB ? 0 : (CAUSAL ? tiles_upto(q0 + 2 * BM - 1) : nk_all);
   const int n_kv = max(nA, nB);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -226,9 +240,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     regs_dec<kRegsOther>();
-    const int row0 = (int)seq_start;
+    const int row0 = (int)seq_start, krow0 = (int)kv_start;
     const int hkv = h / p.G;  // the K / V head this query head reads
-    if (lane == 0) {
+    // n_kv = 0 (a query tile without keys): nothing is loaded or computed.
+    if (lane == 0 && n_kv > 0) {
       mbar_expect_tx(q_full, (hasB ? 2 : 1) * C::Q_BYTES);
       for (int x = 0; x < (hasB ? 2 : 1); ++x)
 #pragma unroll
@@ -244,7 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c)
           tma_load_3d(smem + C::OFF_K + st * C::KV_BYTES + c * BN * C::SWB, &tm_k, &k_full[st],
-                      c * C::CHUNK, hkv, row0 + j * BN);
+                      c * C::CHUNK, hkv, krow0 + j * BN);
       }
     } else if (lane == 1) {
       for (int j = 0; j < n_kv; ++j) {
@@ -256,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c)
           tma_load_3d(smem + C::OFF_V + st * C::KV_BYTES + c * BN * C::SWB, &tm_v, &v_full[st],
-                      c * C::CHUNK, hkv, row0 + j * BN);
+                      c * C::CHUNK, hkv, krow0 + j * BN);
       }
     }
   } else if (warp == 9) {
@@ -294,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16_ts(dt, pt + kk * 8, dv + (uint32_t)((kk * 16 * C::SWB) >> 4), IDESC_O,
                       (j > 0 || kk > 0) ? 1u : 0u);
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, 4);
+      bool ok = n_kv > 0 && mbar_wait(q_full, 0, abort_flag, p.status, 4);
       // Prologue: S_A(0), S_B(0).
       if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, 5);
       if (ok) {
@@ -376,9 +391,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       SCREE_TRACE_ADD(22, t_ld - t_sm0);
 #endif
       const int k0 = j * BN;
-      const bool need_mask = (k0 + BN > L) || (CAUSAL && k0 + BN - 1 > qt0);
+      const bool need_mask = (k0 + BN > Lk) || (CAUSAL && k0 + BN - 1 > qt0 + cdelta);
       if (need_mask) {
-        const int lim = CAUSAL ? min(L - 1, qi) : (L - 1);  // last valid key
+        const int lim = CAUSAL ? min(Lk - 1, qi + cdelta) : (Lk - 1);  // last valid key
 #pragma unroll
         for (int c = 0; c < BN; ++c)
           if (k0 + c > lim) s[c] = -INFINITY;
@@ -485,7 +500,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && nmine > 0) {
       tc_fence_after();
       const bool row_ok = qi < L;
-      const float inv_l = 1.0f / l;
+      // l = 0: a query with no key at all (KV-cache attention with fewer keys
+      // than queries, causal) gets O = 0 and LSE = -inf.
+      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
       T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -505,7 +522,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (row_ok && p.lse != nullptr)
-        p.lse[(seq_start + qi) * p.H + h] = (m_used + log2f(l)) * 0.69314718055994531f;
+        p.lse[(seq_start + qi) * p.H + h] =
+            l > 0.f ? (m_used + log2f(l)) * 0.69314718055994531f : -INFINITY;
+    }
+    if (ok && nmine == 0 && qi < L) {  // no key tile at all for this query tile
+      T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
+#pragma unroll
+      for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
+      if (p.lse != nullptr) p.lse[(seq_start + qi) * p.H + h] = -INFINITY;
     }
   }
 
@@ -566,13 +590,14 @@ extern "C" int scree_attn_fwd(const void* q, const void* k, const void* v, int64
                             workspace, workspace_bytes, stream);
 }
 
-extern "C" int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, int64_t q_rs,
-                                  int64_t q_hs, int64_t k_rs, int64_t k_hs, int64_t v_rs,
-                                  int64_t v_hs, const void* offsets, int offs_is_i64, int64_t B,
-                                  int64_t T, int64_t H, int64_t H_kv, int D, int dtype,
-                                  int causal, float scale, int64_t max_seqlen, void* o,
-                                  int64_t o_rs, int64_t o_hs, float* lse, void* workspace,
-                                  size_t workspace_bytes, void* stream) {
+namespace scree {
+namespace {
+int run_fwd(const void* q, const void* k, const void* v, int64_t q_rs, int64_t q_hs, int64_t k_rs,
+            int64_t k_hs, int64_t v_rs, int64_t v_hs, const void* offsets,
+            const void* offsets_k, int offs_is_i64, int64_t B, int64_t T, int64_t Tk, int64_t H,
+            int64_t H_kv, int D, int dtype, int causal, float scale, int64_t max_seqlen, void* o,
+            int64_t o_rs, int64_t o_hs, float* lse, void* workspace, size_t workspace_bytes,
+            void* stream) {
   (void)max_seqlen;
   SCREE_CHECK_ARG(H_kv >= 1 && H % H_kv == 0,
                   "attn_fwd: query heads (%lld) must be a multiple of K/V heads (%lld)",
@@ -604,8 +629,11 @@ extern "C" int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, i
   CUtensorMap tq, tk, tv;
   int rc;
   if ((rc = make_thd_map(&tq, q, T, H, D, q_rs, q_hs, swb / 2, BM, swb, bf16))) return rc;
-  if ((rc = make_thd_map(&tk, k, T, H_kv, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
-  if ((rc = make_thd_map(&tv, v, T, H_kv, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
+  if (Tk == 0) Tk = 1;  // keys all empty: a 1-row map that no tile reads
+  if ((rc = make_thd_map(&tk, k, Tk, H_kv, D, k_rs, k_hs, swb / 2, BN, swb, bf16))) return rc;
+  if ((rc = make_thd_map(&tv, v, Tk, H_kv, D, v_rs, v_hs, swb / 2, BN, swb, bf16))) return rc;
+  if (offsets_k != nullptr && (rc = launch_validate_offsets(offsets_k, offs_is_i64, B, Tk, s)))
+    return rc;
   if ((rc = launch_build_schedule(offsets, offs_is_i64, B, T, ROWS, (int)H, workspace, s))) return rc;
   FwdParams p;
   p.offs = offsets;
@@ -615,6 +643,7 @@ extern "C" int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, i
   p.T = (int)T;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.sched = workspace;
+  p.offs_k = offsets_k;
   p.B = B;
   p.status = device_status_ptr();
   p.o = o;
@@ -636,6 +665,38 @@ extern "C" int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, i
   SCREE_FWD_CASE(32)
 #undef SCREE_FWD_CASE
   return SCREE_ERR_UNSUPPORTED;
+}
+}  // namespace
+}  // namespace scree
+
+extern "C" int scree_attn_fwd_gqa(const void* q, const void* k, const void* v, int64_t q_rs,
+                                  int64_t q_hs, int64_t k_rs, int64_t k_hs, int64_t v_rs,
+                                  int64_t v_hs, const void* offsets, int offs_is_i64, int64_t B,
+                                  int64_t T, int64_t H, int64_t H_kv, int D, int dtype,
+                                  int causal, float scale, int64_t max_seqlen, void* o,
+                                  int64_t o_rs, int64_t o_hs, float* lse, void* workspace,
+                                  size_t workspace_bytes, void* stream) {
+  return run_fwd(q, k, v, q_rs, q_hs, k_rs, k_hs, v_rs, v_hs, offsets, nullptr, offs_is_i64, B, T,
+                 T, H, H_kv, D, dtype, causal, scale, max_seqlen, o, o_rs, o_hs, lse, workspace,
+                 workspace_bytes, stream);
+}
+
+extern "C" int scree_attn_fwd_kv(const void* q, const void* k, const void* v, int64_t q_rs,
+                                 int64_t q_hs, int64_t k_rs, int64_t k_hs, int64_t v_rs,
+                                 int64_t v_hs, const void* offsets_q, const void* offsets_k,
+                                 int offs_is_i64, int64_t B, int64_t Tq, int64_t Tk, int64_t H,
+                                 int64_t H_kv, int D, int dtype, int causal, float scale, void* o,
+                                 int64_t o_rs, int64_t o_hs, float* lse, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  SCREE_CHECK_ARG(offsets_k != nullptr, "attn_fwd_kv: null key offsets");
+  SCREE_CHECK_ARG(Tk >= 0 && Tk < (1ll << 31), "attn_fwd_kv: bad key row count");
+  if (dtype == SCREE_F32) {
+    set_last_error("attn_fwd_kv: fp16 / bf16 only");
+    return SCREE_ERR_UNSUPPORTED;
+  }
+  return run_fwd(q, k, v, q_rs, q_hs, k_rs, k_hs, v_rs, v_hs, offsets_q, offsets_k, offs_is_i64, B,
+                 Tq, Tk, H, H_kv, D, dtype, causal, scale, 0, o, o_rs, o_hs, lse, workspace,
+                 workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -103,6 +103,45 @@ __global__ void __launch_bounds__(kThreads) to_padded_kernel(
   }
 }
 
+// ---------------------------------------------------------------- kv append
+// out sequence b = cache rows of b, then new rows of b; out_offs[b] =
+// cache_offs[b] + new_offs[b] (prefix sums of the summed lengths), written by
+// the CTAs of chunk 0.  Sequences whose rows fall outside their buffers are
+// skipped and reported.
+template <int W>
+__global__ void __launch_bounds__(kThreads) kv_append_kernel(
+    const void* __restrict__ cache, const void* coffs, const void* __restrict__ fresh,
+    const void* noffs, int is64, int64_t B, int64_t Tc, int64_t Tn, int64_t row_bytes,
+    int rows_per_cta, void* __restrict__ out, int64_t* __restrict__ out_offs, int* status) {
+  using V = typename Vec<W>::T;
+  const uint32_t vpr = (uint32_t)(row_bytes / W);
+  for (int64_t b = blockIdx.y; b < B; b += gridDim.y) {
+    const int64_t cs = load_offset(coffs, is64, b), ce = load_offset(coffs, is64, b + 1);
+    const int64_t ns = load_offset(noffs, is64, b), ne = load_offset(noffs, is64, b + 1);
+    if (cs < 0 || ce < cs || ce > Tc || ns < 0 || ne < ns || ne > Tn) {
+      if (threadIdx.x == 0) record_device_error(status, SCREE_DEVERR_BAD_INPUT, 47);
+      continue;
+    }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      out_offs[b + 1] = ce + ne;
+      if (b == 0) out_offs[0] = 0;
+    }
+    const int64_t lc = ce - cs, len = lc + (ne - ns);
+    const int64_t j0 = (int64_t)blockIdx.x * rows_per_cta;
+    if (j0 >= len) continue;
+    const uint32_t nrows = (uint32_t)(rows_per_cta < len - j0 ? rows_per_cta : len - j0);
+    V* __restrict__ dp = reinterpret_cast<V*>(out) + (cs + ns + j0) * vpr;
+    const V* __restrict__ cp = reinterpret_cast<const V*>(cache) + cs * vpr;
+    const V* __restrict__ np = reinterpret_cast<const V*>(fresh) + (ns - lc) * vpr;
+    const uint32_t n = nrows * vpr;
+    for (uint32_t v = threadIdx.x; v < n; v += blockDim.x) {
+      const int64_t j = j0 + v / vpr;
+      const int64_t e = j * vpr + (v % vpr);
+      dp[v] = j < lc ? cp[e] : np[e];
+    }
+  }
+}
+
 // ---------------------------------------------------------------- from_padded
 // Step 1a: one CTA per padded row writes its mask count into offsets[b+1].
 template <typename MT>
@@ -328,6 +367,29 @@ extern "C" int scree_from_padded(const void* padded, const int32_t* offsets, int
   const dim3 grid = gather_grid(max_len, B, row_bytes, &rpc);
   DISPATCH_WIDTH(w, from_padded_kernel, grid, s, padded, offsets, B, max_len, row_bytes, rpc,
                  values);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
+extern "C" int scree_kv_append(const void* cache, const void* cache_offsets, const void* fresh,
+                               const void* fresh_offsets, int offs_is_i64, int64_t B, int64_t Tc,
+                               int64_t Tn, int64_t max_rows, int64_t row_bytes, void* out,
+                               int64_t* out_offsets, void* stream) {
+  SCREE_CHECK_ARG(B >= 1 && Tc >= 0 && Tn >= 0 && row_bytes >= 0, "scree_kv_append: bad sizes");
+  SCREE_CHECK_ARG(cache_offsets && fresh_offsets && out_offsets, "scree_kv_append: null offsets");
+  SCREE_CHECK_ARG(row_bytes < (1ll << 31), "scree_kv_append: rows larger than 2 GB");
+  SCREE_CHECK_ARG(Tc + Tn == 0 || (out && (Tc == 0 || cache) && (Tn == 0 || fresh)),
+                  "scree_kv_append: null buffer");
+  const int w = row_bytes == 0 ? 1
+                               : pick_width(row_bytes, {(uintptr_t)out, (uintptr_t)cache,
+                                                        (uintptr_t)fresh});
+  SCREE_BIND_DEVICE(stream, out_offsets);
+  cudaStream_t s = (cudaStream_t)stream;
+  int rpc = 1;
+  const int64_t rows = max_rows > 0 ? std::min(max_rows, Tc + Tn) : Tc + Tn;
+  const dim3 grid = gather_grid(std::max<int64_t>(rows, 1), B, row_bytes == 0 ? w : row_bytes, &rpc);
+  DISPATCH_WIDTH(w, kv_append_kernel, grid, s, cache, cache_offsets, fresh, fresh_offsets,
+                 offs_is_i64, B, Tc, Tn, row_bytes, rpc, out, out_offsets, device_status_ptr());
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }
