@@ -42,12 +42,7 @@ constexpr int BN = 128;  // keys per CTA
 // thread (65,536 / 512); the P/dS warpgroups grow to 152, warpgroup 2 shrinks to
 // 80 and warpgroup 3 to 120: 256 x 152 + 128 x 80 + 128 x 120 = 64,512 <= 65,536.
 constexpr int kThreads = 512;
-#ifndef SCREE_BWD_DQ_RED4
-#define SCREE_BWD_DQ_RED4 0
-#endif
-#ifndef SCREE_BWD_DQ_SKIP
-#define SCREE_BWD_DQ_SKIP 0
-#endif
+
 
 constexpr int kRegsSoftmax = 152, kRegsOther = 80, kRegsDq = 120;
 
@@ -545,35 +540,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         tc_fence_before();
         mbar_arrive(dq_empty);
-#if SCREE_BWD_DQ_RED4
-        // Straight from registers, no shared memory: 4 x 4 transposes within
-        // lane quads (two xor-shuffle rounds) give each lane 4 consecutive
-        // features of one query, added with one 16-byte reduction; a warp
-        // instruction covers 4 query rows x 128 contiguous bytes.
         {
-          const int lane = threadIdx.x & 31;
-          const int i0 = lane & 1, i1 = (lane >> 1) & 1;
-          float* fbase = p.dq_acc + ((row0 + q0) * p.H + hq) * D + (warp - 12) * 32 + (lane & ~3);
-          const int64_t rstride = (int64_t)p.H * D;
-#pragma unroll
-          for (int k = 0; k < BQ / 4; ++k) {
-            float a0 = v[4 * k] * sc, a1 = v[4 * k + 1] * sc, a2 = v[4 * k + 2] * sc, a3 = v[4 * k + 3] * sc;
-            float r0 = __shfl_xor_sync(0xffffffffu, i0 ? a0 : a1, 1);
-            float r1 = __shfl_xor_sync(0xffffffffu, i0 ? a2 : a3, 1);
-            if (i0) { a0 = r0; a2 = r1; } else { a1 = r0; a3 = r1; }
-            r0 = __shfl_xor_sync(0xffffffffu, i1 ? a0 : a2, 2);
-            r1 = __shfl_xor_sync(0xffffffffu, i1 ? a1 : a3, 2);
-            if (i1) { a0 = r0; a1 = r1; } else { a2 = r0; a3 = r1; }
-            const int qq = 4 * k + (lane & 3);
-            if (q0 + qq < L) red_add_v4(fbase + qq * rstride, a0, a1, a2, a3);
-          }
-        }
-        if (false) {
-#elif SCREE_BWD_DQ_SKIP
-        if (false) {
-#else
-        {
-#endif
         // Stage the scaled dQ tile as [BQ][D] fp32 and add it into dq_acc with one
         // TMA reduce.  Queries >= L carry exact zeros (their dS is 0), so adding
         // the whole box is safe even where it overlaps the next sequence.
