@@ -194,9 +194,12 @@ class GatherPlan:
 
         return dist.get_global_rank(self.group, r) if self.group is not None else r
 
-    def run(self, tensors):
+    def run(self, tensors, defer: bool = False):
         """All ranks pass their local (T_r, ...) tensors; rank 0 gets the global
-        (T, ...) tensors back, other ranks None."""
+        (T, ...) tensors back, other ranks None.  With ``defer`` the pending
+        requests are returned too, ``(outs, reqs)``: the transfer then overlaps
+        whatever the caller enqueues next, and the caller waits on ``reqs``
+        before it uses the outputs or frees the inputs."""
         import torch
         import torch.distributed as dist
 
@@ -216,6 +219,8 @@ class GatherPlan:
         if self.rank == 0 and self.own_rows.numel():
             for o, t in zip(outs, tensors):
                 o.index_copy_(0, self.own_rows, t)
+        if defer:
+            return outs, reqs
         for q in reqs:
             q.wait()
         return outs
