@@ -401,7 +401,7 @@ def measure_prenorm_qkv(steps, warmup):
     tf = 2.0 * T * C * N / (ms / 1e3) / 1e12
     return {"workload": f"x ({T}, {C}) bf16 (cfg3 rows), Wqkv ({C}, {N}), gamma fp32; y = rmsnorm(x) * gamma @ Wqkv",
             "ms": ms, "tflops": tf, "frac": tf / peak, "peak_tflops": peak,
-            "peak_source": f"{kind} bf16_tflops (burst)", "note": "GEMM kernel time; the gamma-folding pass over the weight (C x N) is a separate launch"}
+            "peak_source": f"{kind} bf16_tflops (burst)", "note": "GEMM kernel time; the row-statistics pass (T x C read) and the gamma-folding pass over the weight (C x N) are separate launches"}
 
 
 def run_norm_suite(args):

@@ -217,13 +217,14 @@ int scree_layernorm_bwd(const void* dy, const void* x, const void* weight, int w
  * stride x_row_stride (elements), weight (C, N) row-major (the reference's
  * Wqkv, used as h @ Wqkv), y (T, N) contiguous in x's dtype (fp16 / bf16), so
  * y viewed as (T, 3, H, D) gives the packed q / k / v of the attention call.
- * rstd (T,) fp32 or NULL.  gamma (C,) in g_dtype or NULL (no weight); with
- * gamma the workspace (scree_rmsnorm_qkv_workspace_size bytes) receives
- * gamma-scaled weight rows.  C must be a multiple of 64 and N of 128.
+ * rstd (T,) fp32 or NULL (then kept in the workspace).  gamma (C,) in g_dtype
+ * or NULL (no weight).  workspace: scree_rmsnorm_qkv_workspace_size bytes
+ * (the gamma-scaled weight rows and the rstd scratch).  A row-statistics pass
+ * precedes the GEMM.  C must be a multiple of 64 and N of 128.
  * Replaces the caller-side sequence of scree/examples/03_train_step.py:36-41
  * (varlen_rmsnorm then a matmul), which has no kernel of its own in the
  * reference. */
-size_t scree_rmsnorm_qkv_workspace_size(int64_t C, int64_t N);
+size_t scree_rmsnorm_qkv_workspace_size(int64_t T, int64_t C, int64_t N);
 int scree_rmsnorm_qkv_fwd(const void* x, int64_t x_row_stride, const void* gamma, int g_dtype,
                           const void* weight, void* y, float* rstd, int64_t T, int64_t C,
                           int64_t N, int dtype, float eps, void* workspace,

@@ -71,7 +71,7 @@ _SIGNATURES = {
     "scree_rmsnorm_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _L, _L, _I, _P, _S, _P]),
     "scree_layernorm_fwd": (_I, [_P, _L, _P, _P, _I, _P, _L, _P, _P, _L, _L, _I, _F, _P]),
     "scree_layernorm_bwd": (_I, [_P, _P, _P, _I, _P, _P, _P, _P, _P, _L, _L, _I, _P, _S, _P]),
-    "scree_rmsnorm_qkv_workspace_size": (_S, [_L, _L]),
+    "scree_rmsnorm_qkv_workspace_size": (_S, [_L, _L, _L]),
     "scree_rmsnorm_qkv_fwd": (_I, [_P, _L, _P, _I, _P, _P, _P, _L, _L, _L, _I, _F, _P, _S, _P]),
     "scree_softmax_fwd": (_I, [_P, _P, _I, _L, _L, _L, _I, _P, _P]),
     "scree_softmax_bwd": (_I, [_P, _P, _P, _I, _L, _L, _L, _I, _P, _P]),

@@ -6,20 +6,20 @@
 // RMSNorm is a per-row scale, so
 //   qkv[t, n] = rstd[t] * sum_c x[t, c] * (gamma[c] * Wqkv[c, n]),
 //   rstd[t]   = 1 / sqrt(mean_c x[t, c]^2 + eps).
-// One GEMM kernel computes it: the raw x tiles feed tcgen05.mma straight from
-// the TMA ring, the four epilogue warps read the same shared-memory x tiles to
-// accumulate each row's sum of squares while the tensor core works, and the
-// epilogue scales the fp32 accumulator row by rstd before the 16-bit store.  x
-// is read from HBM once and the normalised h never exists in memory.  gamma is
-// folded into the weight once per call (gamma[c] * Wqkv[c, :], a C x N pass);
-// with gamma = NULL the weight is used as is.
+// A row-statistics pass writes rstd (one warp per row), then one GEMM kernel:
+// the raw x tiles feed tcgen05.mma straight from the TMA ring and the epilogue
+// scales the fp32 accumulator row by rstd before the 16-bit store, so the
+// normalised h never exists in memory.  gamma is folded into the weight once
+// per call (gamma[c] * Wqkv[c, :], a C x N pass); with gamma = NULL the weight
+// is used as is.  (Taking the sums of squares inside the GEMM, from the staged
+// x tiles, added 16 KB of shared-memory reads to every 48 KB stage of a kernel
+// whose shared-memory port is its limit: 0.58 of the burst GEMM peak against
+// the separate pass's x re-read of T x C x 2 bytes.)
 //
 // Tile: 128 rows x BNT (= 256 or 128) columns per CTA, K in steps of 64
 // (128-byte swizzled rows), a 4-stage TMA ring.  Warp 0 issues TMA, warp 1 the
-// MMAs (M = 128, N = BNT, accumulator in TMEM), warps 2-5 are the row-statistics
-// and epilogue warps (warp w owns TMEM lanes 32 (w % 4) ..).  Stage s is free
-// again when the MMAs that read it completed (commit) and all 128 statistics
-// threads read their rows (mbarrier count 129).
+// MMAs (M = 128, N = BNT, accumulator in TMEM), warps 2-5 are the epilogue
+// warps (warp w owns TMEM lanes 32 (w % 4) ..).
 #include <algorithm>
 #include "attn_common.cuh"
 
@@ -45,7 +45,7 @@ struct QParams {
   int64_t T, N, C;
   float eps;
   void* y;           // (T, N) row-major, dtype
-  float* rstd;       // (T,) or nullptr
+  const float* rstd; // (T,), from the statistics pass
   int* status;
 };
 
@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < QSTAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + 128);  // MMA commit + the 128 statistics threads
+      mbar_init(&empty[s], 1);  // the MMA commit
     }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -128,41 +128,19 @@ __global__ void __launch_bounds__(kQThreads, 1)
       umma_commit(acc_full);
     }
   } else {
-    // ------------------------------------------------------------ statistics + epilogue
+    // ------------------------------------------------------------ epilogue
     const int q = warp & 3;            // TMEM lane quarter of this warp
     const int r = q * 32 + lane;       // row within the tile == TMEM lane
-    float ss = 0.f;
     bool ok = true;
-    for (int kt = 0; kt < nk; ++kt) {
-      const int s = kt % QSTAGES;
-      ok = mbar_wait(&full[s], (kt / QSTAGES) & 1, abort_flag, p.status, 72);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      const uint8_t* row = smem + s * Cf::STAGE + r * 128;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {  // 16-byte chunks, 128B-swizzled by row
-        const uint4 w = *reinterpret_cast<const uint4*>(row + ((j ^ (r & 7)) << 4));
-        const T* e = reinterpret_cast<const T*>(&w);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const float f = Cvt<T>::to_f(e[u]);
-          ss = fmaf(f, f, ss);
-        }
-      }
-      // These generic-proxy reads must be ordered before the TMA (async proxy)
-      // refill of the stage that this arrival allows.
-      fence_proxy_async_smem();
-      mbar_arrive(&empty[s]);
-    }
     if (ok) {
       ok = mbar_wait(acc_full, 0, abort_flag, p.status, 73);
       ok = __all_sync(0xffffffff, ok);
     }
     if (ok) {
       tc_fence_after();
-      const float rs = rsqrtf(ss / (float)p.C + p.eps);
       const int64_t t = (int64_t)m0 + r;
       const bool row_ok = t < p.T;
-      if (row_ok && blockIdx.y == 0 && p.rstd != nullptr) p.rstd[t] = rs;
+      const float rs = row_ok ? p.rstd[t] : 0.f;
       T* yrow = reinterpret_cast<T*>(p.y) + t * p.N + n0;
       const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
@@ -190,6 +168,30 @@ __global__ void __launch_bounds__(kQThreads, 1)
     tc_fence_after();
     tmem_dealloc<BNT>(tmem);
   }
+}
+
+// rstd[t] = 1 / sqrt(mean(x[t]^2) + eps): one warp per row, 16-byte loads.
+template <typename T>
+__global__ void __launch_bounds__(256) row_rstd_kernel(const T* __restrict__ x, int64_t rs_x,
+                                                       int64_t rows, int64_t C, float eps,
+                                                       float* __restrict__ rstd) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * rs_x);
+  float ss = 0.f;
+  for (int64_t v = lane; v < C / 8; v += 32) {
+    const uint4 w = xr[v];
+    const T* e = reinterpret_cast<const T*>(&w);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float f = Cvt<T>::to_f(e[u]);
+      ss = fmaf(f, f, ss);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) rstd[row] = rsqrtf(ss / (float)C + eps);
 }
 
 // W'[c][n] = gamma[c] * W[c][n], rounded to the weight's dtype.
@@ -256,8 +258,11 @@ int launch_qkv(const CUtensorMap& tx, const CUtensorMap& tw, const QParams& p, c
 
 using namespace scree;
 
-extern "C" size_t scree_rmsnorm_qkv_workspace_size(int64_t C, int64_t N) {
-  return (size_t)C * N * 2;
+// Workspace: [gamma-folded weight, C x N x 2 bytes][rstd scratch, T x 4 bytes].
+static size_t qkv_ws_rstd_off(int64_t C, int64_t N) { return ((size_t)C * N * 2 + 255) & ~size_t(255); }
+
+extern "C" size_t scree_rmsnorm_qkv_workspace_size(int64_t T, int64_t C, int64_t N) {
+  return qkv_ws_rstd_off(C, N) + (size_t)T * 4;
 }
 
 extern "C" int scree_rmsnorm_qkv_fwd(const void* x, int64_t x_row_stride, const void* gamma,
@@ -281,9 +286,9 @@ extern "C" int scree_rmsnorm_qkv_fwd(const void* x, int64_t x_row_stride, const 
   cudaStream_t s = (cudaStream_t)stream;
   const bool bf16 = dtype == SCREE_BF16;
   const void* w = weight;
+  SCREE_CHECK_ARG(workspace && workspace_bytes >= scree_rmsnorm_qkv_workspace_size(T, C, N),
+                  "rmsnorm_qkv: workspace too small");
   if (gamma != nullptr) {  // fold gamma into the weight rows once
-    SCREE_CHECK_ARG(workspace && workspace_bytes >= (size_t)C * N * 2,
-                    "rmsnorm_qkv: workspace too small");
     SCREE_CHECK_ARG(g_dtype == SCREE_F16 || g_dtype == SCREE_BF16 || g_dtype == SCREE_F32,
                     "rmsnorm_qkv: gamma dtype");
     const int64_t n = C * N / 8;
@@ -304,7 +309,16 @@ extern "C" int scree_rmsnorm_qkv_fwd(const void* x, int64_t x_row_stride, const 
   if ((rc = make_2d_map(&tx, x, C, T, x_row_stride, QK, QM, bf16))) return rc;
   const int bnt = (N % 256 == 0) ? 256 : 128;
   if ((rc = make_2d_map(&tw, w, N, C, N, 64, QK, bf16))) return rc;
-  QParams p{T, N, C, eps, y, rstd, device_status_ptr()};
+  float* rs = rstd != nullptr ? rstd
+                              : reinterpret_cast<float*>((char*)workspace + qkv_ws_rstd_off(C, N));
+  if (bf16)
+    row_rstd_kernel<__nv_bfloat16><<<(unsigned)((T + 7) / 8), 256, 0, s>>>(
+        (const __nv_bfloat16*)x, x_row_stride, T, C, eps, rs);
+  else
+    row_rstd_kernel<__half><<<(unsigned)((T + 7) / 8), 256, 0, s>>>((const __half*)x, x_row_stride,
+                                                                     T, C, eps, rs);
+  SCREE_LAUNCH_CHECK();
+  QParams p{T, N, C, eps, y, rs, device_status_ptr()};
   ProfScope prof(PROF_NORM_FWD, s);
   if (bf16)
     return bnt == 256 ? launch_qkv<__nv_bfloat16, 256>(tx, tw, p, s)

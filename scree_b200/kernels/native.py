@@ -496,16 +496,15 @@ def rmsnorm_qkv(x, gamma, weight, eps: float = 1e-6, want_rstd: bool = False):
     y = torch.empty((T, N), dtype=x.dtype, device=x.device)
     rstd = torch.empty(T, dtype=torch.float32, device=x.device) if want_rstd else None
     lib = _lib.load()
-    ws = None
     if gamma is not None:
         assert gamma.shape == (C,) and gamma.device == x.device
         gamma = gamma.contiguous()
-        ws = torch.empty(lib.scree_rmsnorm_qkv_workspace_size(C, N), dtype=torch.uint8, device=x.device)
+    ws = torch.empty(lib.scree_rmsnorm_qkv_workspace_size(T, C, N), dtype=torch.uint8, device=x.device)
     with torch.cuda.device(x.device):
         rc = lib.scree_rmsnorm_qkv_fwd(
             x.data_ptr(), x.stride(0), _ptr(gamma), _wcode(gamma, x), weight.data_ptr(), y.data_ptr(),
-            _ptr(rstd), T, C, N, _lib.dtype_code(x.dtype), float(eps), _ptr(ws),
-            ws.numel() if ws is not None else 0, _lib.stream_ptr(x.device),
+            _ptr(rstd), T, C, N, _lib.dtype_code(x.dtype), float(eps), ws.data_ptr(), ws.numel(),
+            _lib.stream_ptr(x.device),
         )
     _lib.check(rc, "rmsnorm_qkv")
     return (y, rstd) if want_rstd else y
