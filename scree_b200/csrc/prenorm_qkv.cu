@@ -16,10 +16,11 @@
 // whose shared-memory port is its limit: 0.58 of the burst GEMM peak against
 // the separate pass's x re-read of T x C x 2 bytes.)
 //
-// Tile: 128 rows x BNT (= 256 or 128) columns per CTA, K in steps of 64
-// (128-byte swizzled rows), a 4-stage TMA ring.  Warp 0 issues TMA, warp 1 the
-// MMAs (M = 128, N = BNT, accumulator in TMEM), warps 2-5 are the epilogue
-// warps (warp w owns TMEM lanes 32 (w % 4) ..).
+// Tiles: 128 rows x BNT (= 256 or 128) columns, K in steps of 64 (128-byte
+// swizzled rows), a 4-stage TMA ring; one persistent CTA per SM walks its tiles
+// with the accumulator double-buffered in TMEM.  Warp 0 issues TMA, warp 1 the
+// MMAs (M = 128, N = BNT), warps 2-5 are the epilogue warps (warp w owns TMEM
+// lanes 32 (w % 4) ..).
 #include <algorithm>
 #include "attn_common.cuh"
 
@@ -57,9 +58,13 @@ __global__ void __launch_bounds__(kQThreads, 1)
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   // A = x tile (K-major), B = weight tile [K rows][N] (N contiguous: MN-major).
   constexpr uint32_t IDESC = make_idesc_f16(QM, BNT, kBF16, false, true);
-  const int m0 = blockIdx.x * QM;
-  const int n0 = blockIdx.y * BNT;
+  // Persistent: CTA c takes tiles c, c + gridDim.x, ...; tile t covers rows
+  // (t / n_tiles_n) * QM and columns (t % n_tiles_n) * BNT.  The accumulator is
+  // double-buffered in TMEM (2 x BNT columns), so the epilogue of one tile runs
+  // while the tensor core works on the next.
   const int nk = (int)(p.C / QK);
+  const int n_tiles_n = (int)(p.N / BNT);
+  const int64_t n_tiles = ((p.T + QM - 1) / QM) * n_tiles_n;
   if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -68,8 +73,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cf::OFF_BAR);
   uint64_t* full = bars;                 // [QSTAGES]
   uint64_t* empty = full + QSTAGES;      // [QSTAGES]
-  uint64_t* acc_full = empty + QSTAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + QSTAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -78,11 +84,14 @@ __global__ void __launch_bounds__(kQThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);  // the MMA commit
     }
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);     // the MMA commit after a tile's last k-step
+      mbar_init(&acc_empty[b], 128);  // the epilogue threads after reading it
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc<BNT>(tmem_slot);
+  if (warp == 1) tmem_alloc<2 * BNT>(tmem_slot);
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_x);
     tma_prefetch_desc(&tm_w);
@@ -95,58 +104,78 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA
     if (elect_one()) {
-      for (int kt = 0; kt < nk; ++kt) {
-        const int s = kt % QSTAGES;
-        if (kt >= QSTAGES &&
-            !mbar_wait(&empty[s], ((kt / QSTAGES) - 1) & 1, abort_flag, p.status, 70))
-          break;
-        uint8_t* st = smem + s * Cf::STAGE;
-        mbar_expect_tx(&full[s], Cf::STAGE);
-        tma_load_2d(st, &tm_x, &full[s], kt * QK, m0);
+      int64_t g = 0;  // k-steps issued by this CTA (ring position)
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const int m0 = (int)(tile / n_tiles_n) * QM, n0 = (int)(tile % n_tiles_n) * BNT;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int s = (int)(g % QSTAGES);
+          if (g >= QSTAGES &&
+              !(ok = mbar_wait(&empty[s], (uint32_t)(((g / QSTAGES) - 1) & 1), abort_flag, p.status, 70)))
+            break;
+          uint8_t* st = smem + s * Cf::STAGE;
+          mbar_expect_tx(&full[s], Cf::STAGE);
+          tma_load_2d(st, &tm_x, &full[s], kt * QK, m0);
 #pragma unroll
-        for (int j = 0; j < BNT / 64; ++j)  // 64-column chunks of [QK rows][64 N]
-          tma_load_2d(st + Cf::A_BYTES + j * QK * 128, &tm_w, &full[s], n0 + j * 64, kt * QK);
+          for (int j = 0; j < BNT / 64; ++j)  // 64-column chunks of [QK rows][64 N]
+            tma_load_2d(st + Cf::A_BYTES + j * QK * 128, &tm_w, &full[s], n0 + j * 64, kt * QK);
+        }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA
     if (elect_one()) {
       bool ok = true;
-      for (int kt = 0; ok && kt < nk; ++kt) {
-        const int s = kt % QSTAGES;
-        if (!(ok = mbar_wait(&full[s], (kt / QSTAGES) & 1, abort_flag, p.status, 71))) break;
+      int64_t g = 0;
+      int i = 0;  // tiles done by this CTA
+      for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !(ok = mbar_wait(&acc_empty[b], (uint32_t)(((i >> 1) - 1) & 1), abort_flag,
+                                       p.status, 74)))
+          break;
         tc_fence_after();
-        const uint32_t a = smem_u32(smem + s * Cf::STAGE);
-        const uint32_t b = a + Cf::A_BYTES;
+        const uint32_t acc = tmem + b * BNT;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int s = (int)(g % QSTAGES);
+          if (!(ok = mbar_wait(&full[s], (uint32_t)((g / QSTAGES) & 1), abort_flag, p.status, 71)))
+            break;
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * Cf::STAGE);
+          const uint32_t bb = a + Cf::A_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < QK / 16; ++kk)
-          umma_f16_ss(tmem, make_sdesc(a + kk * 32, 16, 1024, SW_128B),
-                      make_sdesc(b + kk * 16 * 128, QK * 128, 1024, SW_128B), IDESC,
-                      (kt > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&empty[s]);
+          for (int kk = 0; kk < QK / 16; ++kk)
+            umma_f16_ss(acc, make_sdesc(a + kk * 32, 16, 1024, SW_128B),
+                        make_sdesc(bb + kk * 16 * 128, QK * 128, 1024, SW_128B), IDESC,
+                        (kt > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&acc_full[b]);
       }
-      umma_commit(acc_full);
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;            // TMEM lane quarter of this warp
     const int r = q * 32 + lane;       // row within the tile == TMEM lane
-    bool ok = true;
-    if (ok) {
-      ok = mbar_wait(acc_full, 0, abort_flag, p.status, 73);
-      ok = __all_sync(0xffffffff, ok);
-    }
-    if (ok) {
+    int i = 0;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++i) {
+      const int b = i & 1;
+      bool ok = mbar_wait(&acc_full[b], (uint32_t)((i >> 1) & 1), abort_flag, p.status, 73);
+      if (!__all_sync(0xffffffff, ok)) break;
       tc_fence_after();
+      const int m0 = (int)(tile / n_tiles_n) * QM, n0 = (int)(tile % n_tiles_n) * BNT;
       const int64_t t = (int64_t)m0 + r;
       const bool row_ok = t < p.T;
       const float rs = row_ok ? p.rstd[t] : 0.f;
       T* yrow = reinterpret_cast<T*>(p.y) + t * p.N + n0;
-      const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+      const uint32_t lane_base = tmem + b * BNT + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
       for (int c = 0; c < BNT / 32; ++c) {
         float v[32];
         tmem_ld32_sync(lane_base + c * 32, v);
+        if (c == BNT / 32 - 1) {  // all of this tile's accumulator is in registers
+          tc_fence_before();
+          mbar_arrive(&acc_empty[b]);
+        }
         if (row_ok) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -166,7 +195,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc<BNT>(tmem);
+    tmem_dealloc<2 * BNT>(tmem);
   }
 }
 
@@ -247,7 +276,8 @@ int launch_qkv(const CUtensorMap& tx, const CUtensorMap& tw, const QParams& p, c
                                         QCfg<BNT>::SMEM));
     attr_set[dev & 63] = true;
   }
-  const dim3 grid((unsigned)((p.T + QM - 1) / QM), (unsigned)(p.N / BNT));
+  const int64_t tiles = ((p.T + QM - 1) / QM) * (p.N / BNT);
+  const unsigned grid = (unsigned)std::min<int64_t>(tiles, (int64_t)num_sms());  // persistent
   kern<<<grid, kQThreads, QCfg<BNT>::SMEM, s>>>(tx, tw, p);
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
