@@ -564,6 +564,19 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
 #pragma unroll
     for (int e = 0; e < VW; ++e) accw[i][e] = accb[i][e] = 0.f;
 
+  // The row statistics of block j + 1 are loaded while block j is processed,
+  // so their latency is not exposed when the ring slot is already full.
+  float rs_n[R], mu_n[R];
+  auto load_stats = [&](int64_t blk) {
+#pragma unroll
+    for (int k = 0; k < R; ++k) {
+      const int64_t r = blk * R + k;
+      const bool live = blk < nblocks && r < rows;
+      rs_n[k] = live ? rstd_in[r] : 0.f;
+      mu_n[k] = (LAYER && live) ? mean_in[r] : 0.f;
+    }
+  };
+  load_stats(blockIdx.x);
   int64_t j = 0;
   bool ok = true;
   for (int64_t blk = blockIdx.x; blk < nblocks; blk += gridDim.x, ++j) {
@@ -572,10 +585,10 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
     float rs[R], mu[R];
 #pragma unroll
     for (int k = 0; k < R; ++k) {
-      const bool live = r0 + k < rows;
-      rs[k] = live ? rstd_in[r0 + k] : 0.f;
-      mu[k] = (LAYER && live) ? mean_in[r0 + k] : 0.f;
+      rs[k] = rs_n[k];
+      mu[k] = mu_n[k];
     }
+    load_stats(blk + gridDim.x);
     ok = mbar_wait(&bars[slot], (uint32_t)((j / stages) & 1), &abort_flag, status, kBwdStreamSite);
     ok = __syncthreads_and(ok);
     if (!ok) break;

@@ -72,3 +72,21 @@ def test_softmax_array_level_cfg3(cuda):
     for b in (0, int(np.argmax(lengths))):
         s, e = int(offs[b]), int(offs[b + 1])
         _close(out.values[s:e], oracle.softmax_fwd(to64(x[s:e]), [0, e - s]), torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=str)
+def test_softmax_chunk_boundaries(cuda, dtype):
+    """Sequences at the 128-row chunk and 512-row residency limits of the staged
+    16-bit forward (resident below 513 rows, streamed above), a ragged last
+    column block (F = 200) and a column whose inputs include -inf."""
+    from scree_b200.kernels.native import varlen_softmax_packed
+
+    lengths = [128, 129, 0, 511, 512, 513, 640, 1, 1537]
+    offs = np.concatenate([[0], np.cumsum(lengths)])
+    g = torch.Generator().manual_seed(11)
+    x = (3.0 * torch.randn((offs[-1], 200), generator=g)).to(dtype)
+    x[offs[4] : offs[4] + 7, 5] = float("-inf")
+    x = x.to(cuda)
+    cu = torch.tensor(offs, dtype=torch.int32, device=cuda)
+    y = varlen_softmax_packed(x, cu)
+    _close(y, oracle.softmax_fwd(to64(x), offs), dtype)
