@@ -31,6 +31,7 @@ __global__ void build_schedule_kernel(const void* offs, int is64, int64_t B, int
   __shared__ unsigned long long keys[kSortMax];
   __shared__ long long warp_tot[32];
   __shared__ long long carry;
+  if (threadIdx.x == 0) total_out[1] = 0;  // the persistent kernels' item counter
   if (!offsets_valid_block(offs, is64, B, T)) {
     if (threadIdx.x == 0) {
       *total_out = 0;

@@ -25,7 +25,7 @@ struct SeqRef {
 // sequences with T tokens in total: sum_b ceil(L_b / rows) <= T / rows + B.
 inline int64_t max_tiles(int64_t B, int64_t T, int rows) { return (T + rows - 1) / rows + B; }
 
-// Schedule workspace: [total items (int64, padded to 16 B)] [SeqRef x B].
+// Schedule workspace: [total items (int64)] [item counter (uint64)] [SeqRef x B].
 inline size_t schedule_bytes(int64_t B) { return 16 + sizeof(SeqRef) * (size_t)B; }
 
 // Sequences sorted by length on the device (one CTA) when B <= kSortMax;
@@ -70,6 +70,11 @@ __device__ __forceinline__ WorkItem decode_item(const void* ws, int64_t B, int H
 }
 __device__ __forceinline__ int64_t total_items(const void* ws) {
   return *reinterpret_cast<const int64_t*>(ws);
+}
+// Items handed out so far to persistent CTAs (bytes [8, 16) of the schedule,
+// zeroed by the schedule build that precedes every launch).
+__device__ __forceinline__ unsigned long long* item_counter(const void* ws) {
+  return reinterpret_cast<unsigned long long*>(const_cast<char*>(reinterpret_cast<const char*>(ws)) + 8);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point, so the

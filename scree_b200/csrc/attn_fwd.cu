@@ -30,7 +30,7 @@
 // >= L are computed but never stored.  Rows past T are zero-filled by TMA.
 #ifdef SCREE_TRACE
 // Profiling build only: per-site wait cycles (lane 0 of each waiting warp),
-// [30] = CTA lifetime cycles, [31] = key tiles processed.
+// [30] = CTA lifetime cycles.
 static __device__ unsigned long long g_fwd_trace[32];
 #define SCREE_TRACE_ADD(site, cyc) \
   do { if ((threadIdx.x & 31) == 0 || (site) == 12) atomicAdd(&scree_trace_sm[(site) & 31], (unsigned long long)(cyc)); } while (0)
@@ -58,6 +58,12 @@ constexpr int kRegsSoftmax = 208, kRegsOther = 88;
 #define SCREE_P_PARTS 2
 #endif
 constexpr int kPParts = SCREE_P_PARTS;
+// Work items reach the CTA's roles through a ring of item ids: the K-loading
+// TMA lane takes the next item from the schedule's counter (one atomic per
+// item) and publishes it; the V lane, the MMA thread and the 256 softmax
+// threads read it.
+constexpr int kItemRing = 4;
+constexpr int kItemConsumers = 1 + 1 + 256;
 static_assert(kPParts == 2 || kPParts == 4, "P parts: 2 or 4");
 
 template <int D>
@@ -76,7 +82,7 @@ struct FwdCfg {
   static constexpr int OFF_K = OFF_Q + 2 * Q_BYTES;
   static constexpr int OFF_V = OFF_K + KSTAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_V + VSTAGES * KV_BYTES;
-  static constexpr int OFF_END = OFF_BAR + 256;  // mbarriers, TMEM slot, abort flag
+  static constexpr int OFF_END = OFF_BAR + 512;  // mbarriers, item ring, TMEM slot, abort flag
   static constexpr int SMEM_RAW = OFF_END + 1024 <= 232448 ? OFF_END + 1024 : OFF_END;
   // At least 120 KB so that two CTAs (each holding all 512 TMEM columns) never
   // share an SM.
@@ -142,35 +148,62 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t IDESC_S = make_idesc_f16(BM, BN, kBF16, false, false);
   constexpr uint32_t IDESC_O = make_idesc_f16(BM, D, kBF16, false, true);
 
-  const int64_t item = blockIdx.x;
-  if (item >= total_items(p.sched)) return;
+  // Persistent: one CTA per SM takes items of the longest-first schedule from
+  // a device counter, in order, as its K loads get to them (list scheduling);
+  // every role decodes the items it reads from the CTA's item ring on its own.
+  const int64_t n_items = total_items(p.sched);
+  if ((int64_t)blockIdx.x >= n_items) return;
   // A CTA of an earlier failed launch (or of this one) set the status word: skip.
   if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
-  const WorkItem wi = decode_item(p.sched, p.B, p.H, item);
-  const int h = wi.head;
-  const int64_t seq_start = load_offset(p.offs, p.is64, wi.seq);
-  const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - seq_start);  // query rows
-  // Keys: the same rows, or (KV-cache attention) a sequence of its own; causal
-  // masking is then aligned at the end: query i sees keys <= i + (Lk - L).
-  int64_t kv_start = seq_start;
-  int Lk = L;
-  if (p.offs_k != nullptr) {
-    kv_start = load_offset(p.offs_k, p.is64, wi.seq);
-    Lk = (int)(load_offset(p.offs_k, p.is64, wi.seq + 1) - kv_start);
-  }
-  const int cdelta = Lk - L;
-  // Causal: heaviest (last) 256-row block first within each (sequence, head).
-  const int q0 = (CAUSAL ? (wi.ntiles - 1 - wi.j) : wi.j) * ROWS;
-  const int nk_all = (Lk + BN - 1) / BN;
-  // Key tiles each query tile needs (tile B may not exist at a sequence's end).
-  auto tiles_upto = [&](int last_q) {
-    const int last_k = last_q + cdelta;
-    return last_k < 0 ? 0 : min(nk_all, last_k / BN + 1);
+  // What the producer publishes per item (read from the schedule and the
+  // offsets once, by one thread), and what every role derives from it.
+  struct ItemRec {
+    int64_t seq_start, kv_start;
+    int32_t L, Lk, h, q0;  // L < 0: no items left
   };
-  const int nA = CAUSAL ? tiles_upto(q0 + BM - 1) : nk_all;
-  const bool hasB = q0 + BM < L;
-  const int nB = !hasB ? 0 : (CAUSAL ? tiles_upto(q0 + 2 * BM - 1) : nk_all);
-  const int n_kv = max(nA, nB);
+  struct Geom {
+    int nA, nB, n_kv;
+    bool hasB;
+  };
+  auto load_rec = [&](int64_t item) {
+    ItemRec e;
+    if (item < 0) {
+      e.seq_start = e.kv_start = 0;
+      e.L = e.Lk = -1;
+      e.h = e.q0 = 0;
+      return e;
+    }
+    const WorkItem wi = decode_item(p.sched, p.B, p.H, item);
+    e.h = wi.head;
+    e.seq_start = load_offset(p.offs, p.is64, wi.seq);
+    e.L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - e.seq_start);  // query rows
+    // Keys: the same rows, or (KV-cache attention) a sequence of its own; causal
+    // masking is then aligned at the end: query i sees keys <= i + (Lk - L).
+    e.kv_start = e.seq_start;
+    e.Lk = e.L;
+    if (p.offs_k != nullptr) {
+      e.kv_start = load_offset(p.offs_k, p.is64, wi.seq);
+      e.Lk = (int)(load_offset(p.offs_k, p.is64, wi.seq + 1) - e.kv_start);
+    }
+    // Causal: heaviest (last) 256-row block first within each (sequence, head).
+    e.q0 = (CAUSAL ? (wi.ntiles - 1 - wi.j) : wi.j) * ROWS;
+    return e;
+  };
+  auto derive = [](int L, int Lk, int q0) {
+    Geom g;
+    const int cdelta = Lk - L;
+    const int nk_all = (Lk + BN - 1) / BN;
+    // Key tiles each query tile needs (tile B may not exist at a sequence's end).
+    auto tiles_upto = [&](int last_q) {
+      const int last_k = last_q + cdelta;
+      return last_k < 0 ? 0 : min(nk_all, last_k / BN + 1);
+    };
+    g.nA = CAUSAL ? tiles_upto(q0 + BM - 1) : nk_all;
+    g.hasB = q0 + BM < L;
+    g.nB = !g.hasB ? 0 : (CAUSAL ? tiles_upto(q0 + 2 * BM - 1) : nk_all);
+    g.n_kv = max(g.nA, g.nB);
+    return g;
+  };
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -196,7 +229,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_full + 2;                // [2]
   uint64_t* pv_done = p_full + 2;               // [2]
   uint64_t* p_part = pv_done + 2;               // [2][kPParts - 1] leading parts of P_X
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(p_part + 2 * (kPParts - 1));
+  uint64_t* q_empty = p_part + 2 * (kPParts - 1);  // an item's last S GEMM is done with Q
+  uint64_t* o_empty = q_empty + 1;                 // [2] the epilogue has read O_X
+  uint64_t* item_full = o_empty + 2;               // [kItemRing] an item id is published
+  uint64_t* item_empty = item_full + kItemRing;    // [kItemRing] every role has read it
+  ItemRec* item_ring = reinterpret_cast<ItemRec*>(item_empty + kItemRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_ring + kItemRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -223,6 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&p_full[x], 128);
       for (int q = 0; q + 1 < kPParts; ++q) mbar_init(&p_part[x * (kPParts - 1) + q], 128);
       mbar_init(&pv_done[x], 1);
+      mbar_init(&o_empty[x], 128);
+    }
+    mbar_init(q_empty, 1);
+    for (int k = 0; k < kItemRing; ++k) {
+      mbar_init(&item_full[k], 1);
+      mbar_init(&item_empty[k], kItemConsumers);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -237,48 +281,85 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Record of item k of this CTA from the ring (L < 0: none left); false if the
+  // wait gave up.  `release` = false leaves the slot held (released later by
+  // release_item), so that the record can be read again.
+  auto take_item = [&](int k, ItemRec& e, bool release) -> bool {
+    const int slot = k % kItemRing;
+    if (!mbar_wait(&item_full[slot], (uint32_t)((k / kItemRing) & 1), abort_flag, p.status, 16))
+      return false;
+    e = item_ring[slot];  // ordered after the wait (its asm clobbers memory)
+    if (release) mbar_arrive(&item_empty[slot]);
+    return true;
+  };
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     regs_dec<kRegsOther>();
-    const int row0 = (int)seq_start, krow0 = (int)kv_start;
-    const int hkv = h / p.G;  // the K / V head this query head reads
-    // n_kv = 0 (a query tile without keys): nothing is loaded or computed.
-    if (lane == 0 && n_kv > 0) {
-      mbar_expect_tx(q_full, (hasB ? 2 : 1) * C::Q_BYTES);
-      for (int x = 0; x < (hasB ? 2 : 1); ++x)
-#pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_3d(smem + C::OFF_Q + x * C::Q_BYTES + c * BM * C::SWB, &tm_q, q_full,
-                      c * C::CHUNK, h, row0 + q0 + x * BM);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::KSTAGES;
-        if (j >= C::KSTAGES &&
-            !mbar_wait(&k_empty[st], ((j / C::KSTAGES) - 1) & 1, abort_flag, p.status, 1))
+    // Ring positions run on across items: kc / vc = K / V tiles loaded so far,
+    // qc = items with keys so far (items with n_kv = 0 load and compute nothing).
+    if (lane == 0) {
+      int kc = 0, qc = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k % kItemRing;
+        if (k >= kItemRing &&
+            !(ok = mbar_wait(&item_empty[slot], ((k / kItemRing) - 1) & 1, abort_flag, p.status, 15)))
           break;
-        mbar_expect_tx(&k_full[st], C::KV_BYTES);
+        int64_t item = (int64_t)atomicAdd(item_counter(p.sched), 1ull);
+        if (item >= n_items) item = -1;
+        const ItemRec e = load_rec(item);
+        item_ring[slot] = e;
+        mbar_arrive(&item_full[slot]);  // release: the record is visible to the readers
+        if (item < 0) break;
+        const Geom g = derive(e.L, e.Lk, e.q0);
+        if (g.n_kv == 0) continue;
+        const int row0 = (int)e.seq_start, krow0 = (int)e.kv_start, hkv = e.h / p.G;
+        // Q is overwritten once the previous item's last S GEMM has completed.
+        if (qc > 0 && !(ok = mbar_wait(q_empty, (qc - 1) & 1, abort_flag, p.status, 13))) break;
+        mbar_expect_tx(q_full, (g.hasB ? 2 : 1) * C::Q_BYTES);
+        for (int x = 0; x < (g.hasB ? 2 : 1); ++x)
 #pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_3d(smem + C::OFF_K + st * C::KV_BYTES + c * BN * C::SWB, &tm_k, &k_full[st],
-                      c * C::CHUNK, hkv, krow0 + j * BN);
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_3d(smem + C::OFF_Q + x * C::Q_BYTES + c * BM * C::SWB, &tm_q, q_full,
+                        c * C::CHUNK, e.h, row0 + e.q0 + x * BM);
+        for (int j = 0; j < g.n_kv; ++j, ++kc) {
+          const int st = kc % C::KSTAGES;
+          if (kc >= C::KSTAGES &&
+              !(ok = mbar_wait(&k_empty[st], ((kc / C::KSTAGES) - 1) & 1, abort_flag, p.status, 1)))
+            break;
+          mbar_expect_tx(&k_full[st], C::KV_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_3d(smem + C::OFF_K + st * C::KV_BYTES + c * BN * C::SWB, &tm_k, &k_full[st],
+                        c * C::CHUNK, hkv, krow0 + j * BN);
+        }
+        ++qc;
       }
     } else if (lane == 1) {
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j % C::VSTAGES;
-        if (j >= C::VSTAGES &&
-            !mbar_wait(&v_empty[st], ((j / C::VSTAGES) - 1) & 1, abort_flag, p.status, 12))
-          break;
-        mbar_expect_tx(&v_full[st], C::KV_BYTES);
+      int vc = 0;
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        ItemRec e;
+        if (!(ok = take_item(k, e, true)) || e.L < 0) break;
+        const Geom g = derive(e.L, e.Lk, e.q0);
+        const int krow0 = (int)e.kv_start, hkv = e.h / p.G;
+        for (int j = 0; j < g.n_kv; ++j, ++vc) {
+          const int st = vc % C::VSTAGES;
+          if (vc >= C::VSTAGES &&
+              !(ok = mbar_wait(&v_empty[st], ((vc / C::VSTAGES) - 1) & 1, abort_flag, p.status, 12)))
+            break;
+          mbar_expect_tx(&v_full[st], C::KV_BYTES);
 #pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c)
-          tma_load_3d(smem + C::OFF_V + st * C::KV_BYTES + c * BN * C::SWB, &tm_v, &v_full[st],
-                      c * C::CHUNK, hkv, krow0 + j * BN);
+          for (int c = 0; c < C::NCHUNK; ++c)
+            tma_load_3d(smem + C::OFF_V + st * C::KV_BYTES + c * BN * C::SWB, &tm_v, &v_full[st],
+                        c * C::CHUNK, hkv, krow0 + j * BN);
+        }
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     regs_dec<kRegsOther>();
     if (elect_one()) {
-      const int nX[2] = {nA, nB};
       // Descriptors differ per k-step only in the start address (bits [0,14) =
       // addr >> 4), so they are built once per buffer and advanced by adding
       // the step's byte offset >> 4 (addresses stay below 256 KB: no carry).
@@ -286,8 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int e = kk * 16;
         return (uint32_t)(((e / C::CHUNK) * rows * C::SWB + (e % C::CHUNK) * 2) >> 4);
       };
-      auto issue_s = [&](int x, int j) {
-        const uint32_t kb = sK + (j % C::KSTAGES) * C::KV_BYTES;
+      // S_X = Q_X K^T with K from ring position kpos.
+      auto issue_s = [&](int x, int kpos) {
+        const uint32_t kb = sK + (kpos % C::KSTAGES) * C::KV_BYTES;
         const uint32_t qb = sQ + x * C::Q_BYTES;
         const uint64_t dq = kmajor_desc<D>(qb, BM, 0), dk = kmajor_desc<D>(kb, BN, 0);
         const uint32_t dt = tmem + C::COL_S + x * BN;
@@ -297,10 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                       kk > 0 ? 1u : 0u);
         umma_commit(&s_full[x]);
       };
-      // O_X += P_X(j) V_j over keys [16 kk0, 16 kk1): the first half can run
-      // while the softmax warps are still forming the second.
-      auto issue_pv = [&](int x, int j, int kk0, int kk1) {
-        const uint32_t vb = sV + (j % C::VSTAGES) * C::KV_BYTES;
+      // O_X += P_X(j) V over keys [16 kk0, 16 kk1) with V from ring position
+      // vpos: the first half can run while the softmax warps form the second.
+      auto issue_pv = [&](int x, int j, int vpos, int kk0, int kk1) {
+        const uint32_t vb = sV + (vpos % C::VSTAGES) * C::KV_BYTES;
         const uint32_t pt = tmem + C::COL_S + x * BN;
         const uint64_t dv = v_desc<D>(vb, 0);
         const uint32_t dt = tmem + C::COL_O + x * D;
@@ -309,51 +391,75 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_f16_ts(dt, pt + kk * 8, dv + (uint32_t)((kk * 16 * C::SWB) >> 4), IDESC_O,
                       (j > 0 || kk > 0) ? 1u : 0u);
       };
-      bool ok = n_kv > 0 && mbar_wait(q_full, 0, abort_flag, p.status, 4);
-      // Prologue: S_A(0), S_B(0).
-      if (ok) ok = mbar_wait(&k_full[0], 0, abort_flag, p.status, 5);
-      if (ok) {
+      // kc / vc: ring positions of this item's first K / V tile; sc[x]: S_X
+      // tiles issued so far (= PVs = softmax rounds of tile X); qc: items with keys.
+      int kc = 0, vc = 0, qc = 0;
+      int sc[2] = {0, 0};
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        ItemRec e;
+        if (!(ok = take_item(k, e, true)) || e.L < 0) break;
+        const Geom g = derive(e.L, e.Lk, e.q0);
+        if (g.n_kv == 0) continue;
+        const int nX[2] = {g.nA, g.nB};
+        // Prologue: S_A(0), S_B(0).
+        ok = mbar_wait(q_full, qc & 1, abort_flag, p.status, 4);
+        if (ok) ok = mbar_wait(&k_full[kc % C::KSTAGES], (kc / C::KSTAGES) & 1, abort_flag, p.status, 5);
+        if (!ok) break;
         tc_fence_after();
         for (int x = 0; x < 2; ++x)
-          if (nX[x] > 0) issue_s(x, 0);
-        umma_commit(&k_empty[0]);
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int vst = j % C::VSTAGES;
-        const bool next_k = j + 1 < n_kv;
-        if (!(ok = mbar_wait(&v_full[vst], (j / C::VSTAGES) & 1, abort_flag, p.status, 3))) break;
-        if (next_k) {
-          const int kst = (j + 1) % C::KSTAGES;
-          if (!(ok = mbar_wait(&k_full[kst], ((j + 1) / C::KSTAGES) & 1, abort_flag, p.status, 5)))
+          if (nX[x] > 0) issue_s(x, kc);
+        umma_commit(&k_empty[kc % C::KSTAGES]);
+        if (g.n_kv == 1) umma_commit(q_empty);  // the item's last S GEMMs
+        for (int j = 0; ok && j < g.n_kv; ++j) {
+          const int vpos = vc + j, kn = kc + j + 1;
+          const bool next_k = j + 1 < g.n_kv;
+          if (!(ok = mbar_wait(&v_full[vpos % C::VSTAGES], (vpos / C::VSTAGES) & 1, abort_flag,
+                               p.status, 3)))
             break;
-        }
-        // Per tile X: O_X += P_X(j) V_j as soon as P_X(j) is ready, then
-        // S_X(j+1) into the same TMEM columns (issued after, so executed after).
-        for (int x = 0; x < 2; ++x) {
-          if (j < nX[x]) {
-            constexpr int KK = BN / 16 / kPParts;  // PV k-steps per part of P
-            for (int q = 0; ok && q + 1 < kPParts; ++q) {
-              ok = mbar_wait(&p_part[x * (kPParts - 1) + q], j & 1, abort_flag, p.status, 10 + x);
+          if (next_k &&
+              !(ok = mbar_wait(&k_full[kn % C::KSTAGES], (kn / C::KSTAGES) & 1, abort_flag, p.status, 5)))
+            break;
+          // Per tile X: O_X += P_X(j) V_j as soon as P_X(j) is ready, then
+          // S_X(j+1) into the same TMEM columns (issued after, so executed after).
+          for (int x = 0; x < 2; ++x) {
+            if (j < nX[x]) {
+              const uint32_t ph = (uint32_t)((sc[x] + j) & 1);
+              // O_X is overwritten by the first PV once the previous item's
+              // epilogue has read it.
+              if (j == 0 && qc > 0 &&
+                  !(ok = mbar_wait(&o_empty[x], (qc - 1) & 1, abort_flag, p.status, 14)))
+                break;
+              constexpr int KK = BN / 16 / kPParts;  // PV k-steps per part of P
+              for (int q = 0; ok && q + 1 < kPParts; ++q) {
+                ok = mbar_wait(&p_part[x * (kPParts - 1) + q], ph, abort_flag, p.status, 10 + x);
+                tc_fence_after();
+                if (ok) issue_pv(x, j, vpos, q * KK, (q + 1) * KK);
+              }
+              if (!ok) break;
+              if (!(ok = mbar_wait(&p_full[x], ph, abort_flag, p.status, 2 + 4 * x))) break;
               tc_fence_after();
-              if (ok) issue_pv(x, j, q * KK, (q + 1) * KK);
+#ifdef SCREE_TRACE
+              const long long t_is0 = clock64();
+#endif
+              issue_pv(x, j, vpos, (kPParts - 1) * KK, BN / 16);
+              umma_commit(&pv_done[x]);
+              if (j + 1 < nX[x]) issue_s(x, kn);
+#ifdef SCREE_TRACE
+              SCREE_TRACE_ADD(21, clock64() - t_is0);
+#endif
             }
-            if (!ok) break;
-            if (!(ok = mbar_wait(&p_full[x], j & 1, abort_flag, p.status, 2 + 4 * x))) break;
-            tc_fence_after();
-#ifdef SCREE_TRACE
-            const long long t_is0 = clock64();
-#endif
-            issue_pv(x, j, (kPParts - 1) * KK, BN / 16);
-            umma_commit(&pv_done[x]);
-            if (j + 1 < nX[x]) issue_s(x, j + 1);
-#ifdef SCREE_TRACE
-            SCREE_TRACE_ADD(21, clock64() - t_is0);
-#endif
           }
+          if (!ok) break;
+          if (j + 2 == g.n_kv) umma_commit(q_empty);  // S_X(n_kv - 1) were the last S GEMMs
+          umma_commit(&v_empty[vpos % C::VSTAGES]);
+          if (next_k) umma_commit(&k_empty[kn % C::KSTAGES]);
         }
-        if (!ok) break;
-        umma_commit(&v_empty[vst]);
-        if (next_k) umma_commit(&k_empty[(j + 1) % C::KSTAGES]);
+        kc += g.n_kv;
+        vc += g.n_kv;
+        sc[0] += g.nA;
+        sc[1] += g.nB;
+        ++qc;
       }
     }
   } else if (warp >= 10) {
@@ -366,170 +472,188 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const uint32_t col_s = lane_base + C::COL_S + x * BN;
     const uint32_t col_o = lane_base + C::COL_O + x * D;
-    const int qt0 = q0 + x * BM;              // first row of this tile
-    const int qi = qt0 + r;                   // query index within the sequence
-    const int nmine = x == 0 ? nA : nB;
     const float sl2 = p.scale_log2;
-    float m_used = -INFINITY;                 // running max, scaled log2 units
-    float l = 0.f;
+    int sc = 0;  // softmax rounds of this tile so far (= S_X tiles issued)
     bool ok = true;
-    for (int j = 0; j < nmine; ++j) {
-      ok = mbar_wait(&s_full[x], j & 1, abort_flag, p.status, 7);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-#ifdef SCREE_TRACE
-      const long long t_sm0 = clock64();
-#endif
-      tc_fence_after();
-      // One TMEM load of the whole 128-column row (a single wait::ld).
-      float s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c)
-        tmem_ld32(col_s + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
-      tmem_wait_ld();
-#ifdef SCREE_TRACE
-      const long long t_ld = clock64();
-      SCREE_TRACE_ADD(22, t_ld - t_sm0);
-#endif
-      const int k0 = j * BN;
-      const bool need_mask = (k0 + BN > Lk) || (CAUSAL && k0 + BN - 1 > qt0 + cdelta);
-      if (need_mask) {
-        const int lim = CAUSAL ? min(Lk - 1, qi + cdelta) : (Lk - 1);  // last valid key
-#pragma unroll
-        for (int c = 0; c < BN; ++c)
-          if (k0 + c > lim) s[c] = -INFINITY;
-      }
-      // Row max: 8 independent chains of three-input max (two values per step).
-      float mx8[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) mx8[a] = s[a];
-#pragma unroll
-      for (int c = 8; c < BN; c += 16)
-#pragma unroll
-        for (int a = 0; a < 8; ++a) mx8[a] = fmax3(mx8[a], s[c + a], s[c + 8 + a < BN ? c + 8 + a : c + a]);
-      const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
-                             fmaxf(mx8[6], mx8[7]));
-      const float m_cand = mx * sl2;
-#ifdef SCREE_TRACE
-      const long long t_mx = clock64();
-      SCREE_TRACE_ADD(23, t_mx - t_ld);
-#endif
-      float alpha = 1.f;
-      bool need = false;
-      if (m_used == -INFINITY) {
-        need = true;
-        alpha = 0.f;
-        m_used = m_cand;
-      } else if (m_cand > m_used + 8.0f) {
-        need = true;
-        alpha = ex2_approx(m_used - m_cand);
-        m_used = m_cand;
-      }
-      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
-      // Exponentiate and pack: each pair of S values dies as its packed word appears.
-      // Exponentiate and pack, two columns per packed f32x2 FMA / add; each pair of
-      // S values dies as its packed 16-bit word appears.
-      const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_eff, -m_eff);
-      uint64_t rs4[4] = {0ull, 0ull, 0ull, 0ull};  // (+0.0f, +0.0f) pairs
-      uint32_t pk[BN / 2];
-      // Exponentiate and pack columns [c0, c1), two per packed f32x2 FMA / add;
-      // each pair of S values dies as its packed 16-bit word appears.
-      auto exp_pack = [&](int c0, int c1) {
-#pragma unroll
-        for (int c = c0; c < c1; c += 2) {
-          float x0, x1;
-          f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, negm2), x0, x1);
-          const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
-          const uint64_t e01 = f2_pack(e0, e1);
-          rs4[(c / 2) & 3] = f2_add(rs4[(c / 2) & 3], e01);
-          pk[c / 2] = Pk2<T>::pack(e0, e1);
-        }
-      };
-      constexpr int PC = BN / kPParts;  // keys per part of P
-      auto store_part = [&](int q) {   // packed columns [q PC / 2, (q + 1) PC / 2)
-        if constexpr (PC / 2 == 32)
-          tmem_st32u(col_s + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[q * 32]));
-        else
-          tmem_st16u(col_s + q * 16, &pk[q * 16]);
-      };
-      exp_pack(0, PC);
-      if (j >= 1) {
-        // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
-        // before P_X(j) overwrites the columns it read.  It already is in the
-        // common case: S_X(j) was issued after it and s_full covers both.
-        ok = mbar_wait(&pv_done[x], (j - 1) & 1, abort_flag, p.status, 8);
+    for (int k = 0; ok; ++k) {
+      ItemRec e;
+      ok = __all_sync(0xffffffff, take_item(k, e, false));  // released after the epilogue
+      if (!ok || e.L < 0) break;
+      const Geom g = derive(e.L, e.Lk, e.q0);
+      const int Lk = e.Lk, cdelta = e.Lk - e.L;
+      const int qt0 = e.q0 + x * BM;            // first row of this tile
+      const int qi = qt0 + r;                   // query index within the sequence
+      const int nmine = x == 0 ? g.nA : g.nB;
+      float m_used = -INFINITY;                 // running max, scaled log2 units
+      float l = 0.f;
+      for (int j = 0; j < nmine; ++j) {
+        ok = mbar_wait(&s_full[x], (sc + j) & 1, abort_flag, p.status, 7);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+#ifdef SCREE_TRACE
+        const long long t_sm0 = clock64();
+#endif
         tc_fence_after();
-        if (__any_sync(0xffffffff, need)) {
+        // One TMEM load of the whole 128-column row (a single wait::ld).
+        float s[BN];
 #pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            float o[32];
-            tmem_ld32(col_o + c * 32, o);
-            tmem_wait_ld();
+        for (int c = 0; c < BN / 32; ++c)
+          tmem_ld32(col_s + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+        tmem_wait_ld();
+#ifdef SCREE_TRACE
+        const long long t_ld = clock64();
+        SCREE_TRACE_ADD(22, t_ld - t_sm0);
+#endif
+        const int k0 = j * BN;
+        const bool need_mask = (k0 + BN > Lk) || (CAUSAL && k0 + BN - 1 > qt0 + cdelta);
+        if (need_mask) {
+          const int lim = CAUSAL ? min(Lk - 1, qi + cdelta) : (Lk - 1);  // last valid key
 #pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] *= alpha;
-            tmem_st32(col_o + c * 32, o);
+          for (int c = 0; c < BN; ++c)
+            if (k0 + c > lim) s[c] = -INFINITY;
+        }
+        // Row max: 8 independent chains of three-input max (two values per step).
+        float mx8[8];
+#pragma unroll
+        for (int a = 0; a < 8; ++a) mx8[a] = s[a];
+#pragma unroll
+        for (int c = 8; c < BN; c += 16)
+#pragma unroll
+          for (int a = 0; a < 8; ++a) mx8[a] = fmax3(mx8[a], s[c + a], s[c + 8 + a < BN ? c + 8 + a : c + a]);
+        const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                               fmaxf(mx8[6], mx8[7]));
+        const float m_cand = mx * sl2;
+#ifdef SCREE_TRACE
+        const long long t_mx = clock64();
+        SCREE_TRACE_ADD(23, t_mx - t_ld);
+#endif
+        float alpha = 1.f;
+        bool need = false;
+        if (m_used == -INFINITY) {
+          need = true;
+          alpha = 0.f;
+          m_used = m_cand;
+        } else if (m_cand > m_used + 8.0f) {
+          need = true;
+          alpha = ex2_approx(m_used - m_cand);
+          m_used = m_cand;
+        }
+        const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+        // Exponentiate and pack: each pair of S values dies as its packed word appears.
+        // Exponentiate and pack, two columns per packed f32x2 FMA / add; each pair of
+        // S values dies as its packed 16-bit word appears.
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm2 = f2_pack(-m_eff, -m_eff);
+        uint64_t rs4[4] = {0ull, 0ull, 0ull, 0ull};  // (+0.0f, +0.0f) pairs
+        uint32_t pk[BN / 2];
+        // Exponentiate and pack columns [c0, c1), two per packed f32x2 FMA / add;
+        // each pair of S values dies as its packed 16-bit word appears.
+        auto exp_pack = [&](int c0, int c1) {
+#pragma unroll
+          for (int c = c0; c < c1; c += 2) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(s[c], s[c + 1]), sl2x2, negm2), x0, x1);
+            const float e0 = ex2_approx(x0), e1 = ex2_approx(x1);
+            const uint64_t e01 = f2_pack(e0, e1);
+            rs4[(c / 2) & 3] = f2_add(rs4[(c / 2) & 3], e01);
+            pk[c / 2] = Pk2<T>::pack(e0, e1);
+          }
+        };
+        constexpr int PC = BN / kPParts;  // keys per part of P
+        auto store_part = [&](int q) {   // packed columns [q PC / 2, (q + 1) PC / 2)
+          if constexpr (PC / 2 == 32)
+            tmem_st32u(col_s + q * 32, *reinterpret_cast<uint32_t(*)[32]>(&pk[q * 32]));
+          else
+            tmem_st16u(col_s + q * 16, &pk[q * 16]);
+        };
+        exp_pack(0, PC);
+        if (j >= 1) {
+          // O_X += P_X(j-1) V_{j-1} must be complete before O_X is rescaled and
+          // before P_X(j) overwrites the columns it read.  It already is in the
+          // common case: S_X(j) was issued after it and s_full covers both.
+          ok = mbar_wait(&pv_done[x], (sc + j - 1) & 1, abort_flag, p.status, 8);
+          if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+          tc_fence_after();
+          if (__any_sync(0xffffffff, need)) {
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+              float o[32];
+              tmem_ld32(col_o + c * 32, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] *= alpha;
+              tmem_st32(col_o + c * 32, o);
+            }
           }
         }
-      }
-      // P_X(j) is published part by part: the MMA warp starts O_X += P V on
-      // the first keys while the later ones are formed.
+        // P_X(j) is published part by part: the MMA warp starts O_X += P V on
+        // the first keys while the later ones are formed.
 #pragma unroll
-      for (int q = 0; q + 1 < kPParts; ++q) {
-        store_part(q);
+        for (int q = 0; q + 1 < kPParts; ++q) {
+          store_part(q);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&p_part[x * (kPParts - 1) + q]);
+          exp_pack((q + 1) * PC, (q + 2) * PC);
+        }
+        store_part(kPParts - 1);
+        float ra, rb;
+        f2_unpack(f2_add(f2_add(rs4[0], rs4[1]), f2_add(rs4[2], rs4[3])), ra, rb);
+        l = l * alpha + (ra + rb);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&p_part[x * (kPParts - 1) + q]);
-        exp_pack((q + 1) * PC, (q + 2) * PC);
-      }
-      store_part(kPParts - 1);
-      float ra, rb;
-      f2_unpack(f2_add(f2_add(rs4[0], rs4[1]), f2_add(rs4[2], rs4[3])), ra, rb);
-      l = l * alpha + (ra + rb);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[x]);
+        mbar_arrive(&p_full[x]);
 #ifdef SCREE_TRACE
-      SCREE_TRACE_ADD(20, clock64() - t_sm0);
+        SCREE_TRACE_ADD(20, clock64() - t_sm0);
 #endif
-    }
-    // ------------------------------------------------------------ epilogue
-    if (ok && nmine > 0) {
-      ok = mbar_wait(&pv_done[x], (nmine - 1) & 1, abort_flag, p.status, 9);
-      ok = __all_sync(0xffffffff, ok);
-    }
-    if (ok && nmine > 0) {
-      tc_fence_after();
-      const bool row_ok = qi < L;
-      // l = 0: a query with no key at all (KV-cache attention with fewer keys
-      // than queries, causal) gets O = 0 and LSE = -inf.
-      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
-      T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
+      }
+      // ------------------------------------------------------------ epilogue
+      // The item's record is still held in the ring: re-read what the epilogue
+      // needs rather than keep it in registers through the key loop.
+      const ItemRec& er = item_ring[k % kItemRing];
+      const int L = er.L, h = er.h;
+      const int64_t seq_start = er.seq_start;
+      if (ok && nmine > 0) {
+        ok = mbar_wait(&pv_done[x], (sc + nmine - 1) & 1, abort_flag, p.status, 9);
+        ok = __all_sync(0xffffffff, ok);
+      }
+      if (ok && nmine > 0) {
+        tc_fence_after();
+        const bool row_ok = qi < L;
+        // l = 0: a query with no key at all (KV-cache attention with fewer keys
+        // than queries, causal) gets O = 0 and LSE = -inf.
+        const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+        T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        float o[32];
-        tmem_ld32(col_o + c * 32, o);
-        tmem_wait_ld();
-        if (row_ok) {
+        for (int c = 0; c < D / 32; ++c) {
+          float o[32];
+          tmem_ld32(col_o + c * 32, o);
+          tmem_wait_ld();
+          if (row_ok) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint4 w;
-            w.x = Pk2<T>::pack(o[u * 8 + 0] * inv_l, o[u * 8 + 1] * inv_l);
-            w.y = Pk2<T>::pack(o[u * 8 + 2] * inv_l, o[u * 8 + 3] * inv_l);
-            w.z = Pk2<T>::pack(o[u * 8 + 4] * inv_l, o[u * 8 + 5] * inv_l);
-            w.w = Pk2<T>::pack(o[u * 8 + 6] * inv_l, o[u * 8 + 7] * inv_l);
-            *reinterpret_cast<uint4*>(orow + c * 32 + u * 8) = w;
+            for (int u = 0; u < 4; ++u) {
+              uint4 w;
+              w.x = Pk2<T>::pack(o[u * 8 + 0] * inv_l, o[u * 8 + 1] * inv_l);
+              w.y = Pk2<T>::pack(o[u * 8 + 2] * inv_l, o[u * 8 + 3] * inv_l);
+              w.z = Pk2<T>::pack(o[u * 8 + 4] * inv_l, o[u * 8 + 5] * inv_l);
+              w.w = Pk2<T>::pack(o[u * 8 + 6] * inv_l, o[u * 8 + 7] * inv_l);
+              *reinterpret_cast<uint4*>(orow + c * 32 + u * 8) = w;
+            }
           }
         }
+        tc_fence_before();
+        mbar_arrive(&o_empty[x]);  // O_X is in registers: the next item may overwrite it
+        if (row_ok && p.lse != nullptr)
+          p.lse[(seq_start + qi) * p.H + h] =
+              l > 0.f ? (m_used + log2f(l)) * 0.69314718055994531f : -INFINITY;
       }
-      if (row_ok && p.lse != nullptr)
-        p.lse[(seq_start + qi) * p.H + h] =
-            l > 0.f ? (m_used + log2f(l)) * 0.69314718055994531f : -INFINITY;
-    }
-    if (ok && nmine == 0 && qi < L) {  // no key tile at all for this query tile
-      T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
+      if (ok && nmine == 0 && qi < L) {  // no key tile at all for this query tile
+        T* orow = reinterpret_cast<T*>(p.o) + (seq_start + qi) * p.o_rs + (int64_t)h * p.o_hs;
 #pragma unroll
-      for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
-      if (p.lse != nullptr) p.lse[(seq_start + qi) * p.H + h] = -INFINITY;
+        for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(orow + c * 8) = make_uint4(0, 0, 0, 0);
+        if (p.lse != nullptr) p.lse[(seq_start + qi) * p.H + h] = -INFINITY;
+      }
+      if (ok && nmine == 0 && g.n_kv > 0) mbar_arrive(&o_empty[x]);
+      mbar_arrive(&item_empty[k % kItemRing]);
+      sc += nmine;
     }
   }
 
@@ -539,7 +663,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef SCREE_TRACE
   if (threadIdx.x == 0) {
     scree_trace_sm[30] += (unsigned long long)(clock64() - t_cta0);
-    scree_trace_sm[31] += (unsigned long long)(n_kv);
   }
   __syncthreads();
   if (threadIdx.x < 32) atomicAdd(&g_fwd_trace[threadIdx.x], scree_trace_sm[threadIdx.x]);
@@ -650,8 +773,9 @@ int run_fwd(const void* q, const void* k, const void* v, int64_t q_rs, int64_t q
   p.o_rs = o_rs;
   p.o_hs = o_hs;
   p.lse = lse;
-  const int64_t grid = max_tiles(B, T, ROWS) * H;
-  SCREE_CHECK_ARG(grid < (1ll << 31), "attn_fwd: grid too large");
+  // Persistent CTAs, one per SM (each holds all 512 TMEM columns); the items
+  // themselves are counted on the device.
+  const int64_t grid = std::min<int64_t>(max_tiles(B, T, ROWS) * H, (int64_t)num_sms());
 #define SCREE_FWD_CASE(DD)                                                              \
   if (D == DD) {                                                                        \
     if (bf16)                                                                           \
