@@ -24,7 +24,7 @@
 #include <algorithm>
 #ifdef SCREE_TRACE
 // Profiling build only: per-site wait cycles (lane 0 of each waiting warp),
-// [62] = CTA lifetime cycles, [63] = query tiles processed.
+// [62] = CTA lifetime cycles.
 static __device__ unsigned long long g_bwd_trace[64];
 #define SCREE_TRACE_ADD(site, cyc) \
   do { if ((threadIdx.x & 31) == 0 || (site) == 12) atomicAdd(&scree_trace_sm[(site) & 63], (unsigned long long)(cyc)); } while (0)
@@ -45,6 +45,11 @@ constexpr int kThreads = 512;
 
 
 constexpr int kRegsSoftmax = 152, kRegsOther = 80, kRegsDq = 120;
+// Item records reach the roles through a ring: the TMA thread takes the next
+// item from the schedule's counter and publishes it; the MMA thread, the 256
+// P/dS threads and the 128 dQ threads read it.
+constexpr int kItemRing = 4;
+constexpr int kItemConsumers = 1 + 256 + 128;
 
 template <int D>
 struct BwdCfg {
@@ -187,27 +192,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t ID_DQ = C::DQT ? make_idesc_f16(D, BQ, kBF16, true, true)
                                     : make_idesc_f16(BQ, D, kBF16, true, true);
 
-  const int64_t item = blockIdx.x;
-  if (item >= total_items(p.sched)) return;
+  // Persistent: one CTA per SM takes items (128-key tiles of one K / V head)
+  // of the longest-first schedule from a device counter as its TMA producer
+  // gets to them; the producer publishes each item's record through a ring.
+  const int64_t n_items = total_items(p.sched);
+  if ((int64_t)blockIdx.x >= n_items) return;
   // A CTA of an earlier failed launch (or of this one) set the status word: skip.
   if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return;
-  const WorkItem wi = decode_item(p.sched, p.B, p.Hkv, item);
-  const int h = wi.head;  // K / V head; its G query heads are walked in turn
-  const int64_t row0 = load_offset(p.offs, p.is64, wi.seq);
-  const int L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - row0);
-  const int k0 = wi.j * BN;  // causal: the first key tile has the most query tiles
-  const int nq = (L + BQ - 1) / BQ;
-  const int i_first = CAUSAL ? k0 / BQ : 0;
-  const int n_it = nq - i_first;  // >= 1 since k0 < L
-  // Grouped-query attention: the CTA's K / V tile serves G query heads, so it
+  struct ItemRec {
+    int64_t row0;
+    int32_t L, k0, h;  // L < 0: no items left; h: the K / V head
+    int32_t pad;
+  };
+  auto load_rec = [&](int64_t item) {
+    ItemRec e;
+    e.pad = 0;
+    if (item < 0) {
+      e.row0 = 0;
+      e.L = -1;
+      e.k0 = e.h = 0;
+      return e;
+    }
+    const WorkItem wi = decode_item(p.sched, p.B, p.Hkv, item);
+    e.h = wi.head;  // K / V head; its G query heads are walked in turn
+    e.row0 = load_offset(p.offs, p.is64, wi.seq);
+    e.L = (int)(load_offset(p.offs, p.is64, wi.seq + 1) - e.row0);
+    e.k0 = wi.j * BN;  // causal: the first key tile has the most query tiles
+    return e;
+  };
+  // Grouped-query attention: an item's K / V tile serves G query heads, so it
   // walks n_it query tiles for each of them (G = 1: plain attention) and
-  // accumulates dK, dV over all G * n_it tiles.  Iteration `it` below counts
-  // those: query tile i_first + it % n_it of query head h * G + it / n_it.
-  // (Separate instantiation without grouping: the index arithmetic below cost
-  // 6% of the backward when it ran for G = 1 too.)
-  const int n_all = GQA ? n_it * p.G : n_it;
-  auto q_tile = [&](int it_) { return GQA ? i_first + it_ % n_it : i_first + it_; };
-  auto q_head = [&](int it_) { return GQA ? h * p.G + it_ / n_it : h; };
+  // accumulates dK, dV over all G * n_it tiles.  Iteration `it` counts those:
+  // query tile i_first + it % n_it of query head h * G + it / n_it.
+  // (Separate instantiation without grouping: the index arithmetic cost 6% of
+  // the backward when it ran for G = 1 too.)
+  struct Walk {
+    int i_first, n_it, n_all;
+  };
+  auto walk = [&](const ItemRec& e) {
+    Walk w;
+    const int nq = (e.L + BQ - 1) / BQ;
+    w.i_first = CAUSAL ? e.k0 / BQ : 0;
+    w.n_it = nq - w.i_first;  // >= 1 since k0 < L
+    w.n_all = GQA ? w.n_it * p.G : w.n_it;
+    return w;
+  };
+  auto q_tile = [&](const Walk& w, int it_) { return GQA ? w.i_first + it_ % w.n_it : w.i_first + it_; };
+  auto q_head = [&](const ItemRec& e, const Walk& w, int it_) {
+    return GQA ? e.h * p.G + it_ / w.n_it : e.h;
+  };
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -237,7 +270,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* dq_full = ds_free + 1;
   uint64_t* dq_empty = dq_full + 1;
   uint64_t* acc_done = dq_empty + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
+  uint64_t* acc_empty = acc_done + 1;   // the epilogue has read dV, dK
+  uint64_t* kv_empty = acc_empty + 1;   // an item's last MMA is done with K, V
+  uint64_t* item_full = kv_empty + 1;   // [kItemRing]
+  uint64_t* item_empty = item_full + kItemRing;
+  ItemRec* item_ring = reinterpret_cast<ItemRec*>(item_empty + kItemRing);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_ring + kItemRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -263,6 +301,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(acc_done, 1);
+    mbar_init(acc_empty, 256);
+    mbar_init(kv_empty, 1);
+    for (int k = 0; k < kItemRing; ++k) {
+      mbar_init(&item_full[k], 1);
+      mbar_init(&item_empty[k], kItemConsumers);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -277,33 +321,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Record of item k of this CTA from the ring (L < 0: none left); false if the
+  // wait gave up.  `release` = false keeps the slot (released by the caller).
+  auto take_item = [&](int k, ItemRec& e, bool release) -> bool {
+    const int slot = k % kItemRing;
+    if (!mbar_wait(&item_full[slot], (uint32_t)((k / kItemRing) & 1), abort_flag, p.status, 34))
+      return false;
+    e = item_ring[slot];  // ordered after the wait (its asm clobbers memory)
+    if (release) mbar_arrive(&item_empty[slot]);
+    return true;
+  };
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     regs_dec<kRegsOther>();
     if (elect_one()) {
-      mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
-#pragma unroll
-      for (int c = 0; c < C::NCHUNK; ++c) {
-        tma_load_3d(smem + C::OFF_K + c * BN * C::SWB, &tm_k, kv_full, c * C::CHUNK, h,
-                    (int)row0 + k0);
-        tma_load_3d(smem + C::OFF_V + c * BN * C::SWB, &tm_v, kv_full, c * C::CHUNK, h,
-                    (int)row0 + k0);
-      }
-      for (int it = 0; it < n_all; ++it) {
-        const int st = it % C::STAGES;
-        if (it >= C::STAGES &&
-            !mbar_wait(&q_empty[st], ((it / C::STAGES) - 1) & 1, abort_flag, p.status, 21))
+      int gq = 0;  // Q / dO tiles loaded so far (ring position)
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k % kItemRing;
+        if (k >= kItemRing &&
+            !(ok = mbar_wait(&item_empty[slot], ((k / kItemRing) - 1) & 1, abort_flag, p.status, 35)))
           break;
-        const int qrow = (int)row0 + q_tile(it) * BQ;
-        const int hq = q_head(it);
-        mbar_expect_tx(&q_full[st], 2 * C::QT_BYTES);
+        int64_t item = (int64_t)atomicAdd(item_counter(p.sched), 1ull);
+        if (item >= n_items) item = -1;
+        const ItemRec e = load_rec(item);
+        item_ring[slot] = e;
+        mbar_arrive(&item_full[slot]);  // release: the record is visible to the readers
+        if (item < 0) break;
+        const Walk w = walk(e);
+        // K, V are overwritten once the previous item's last MMA has completed.
+        if (k > 0 && !(ok = mbar_wait(kv_empty, (k - 1) & 1, abort_flag, p.status, 36))) break;
+        mbar_expect_tx(kv_full, 2 * C::KV_BYTES);
 #pragma unroll
         for (int c = 0; c < C::NCHUNK; ++c) {
-          tma_load_3d(smem + C::OFF_Q + st * C::QT_BYTES + c * BQ * C::SWB, &tm_q, &q_full[st],
-                      c * C::CHUNK, hq, qrow);
-          tma_load_3d(smem + C::OFF_DO + st * C::QT_BYTES + c * BQ * C::SWB, &tm_do,
-                      &q_full[st], c * C::CHUNK, hq, qrow);
+          tma_load_3d(smem + C::OFF_K + c * BN * C::SWB, &tm_k, kv_full, c * C::CHUNK, e.h,
+                      (int)e.row0 + e.k0);
+          tma_load_3d(smem + C::OFF_V + c * BN * C::SWB, &tm_v, kv_full, c * C::CHUNK, e.h,
+                      (int)e.row0 + e.k0);
+        }
+        for (int it = 0; it < w.n_all; ++it, ++gq) {
+          const int st = gq % C::STAGES;
+          if (gq >= C::STAGES &&
+              !(ok = mbar_wait(&q_empty[st], ((gq / C::STAGES) - 1) & 1, abort_flag, p.status, 21)))
+            break;
+          const int qrow = (int)e.row0 + q_tile(w, it) * BQ;
+          const int hq = q_head(e, w, it);
+          mbar_expect_tx(&q_full[st], 2 * C::QT_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::NCHUNK; ++c) {
+            tma_load_3d(smem + C::OFF_Q + st * C::QT_BYTES + c * BQ * C::SWB, &tm_q, &q_full[st],
+                        c * C::CHUNK, hq, qrow);
+            tma_load_3d(smem + C::OFF_DO + st * C::QT_BYTES + c * BQ * C::SWB, &tm_do,
+                        &q_full[st], c * C::CHUNK, hq, qrow);
+          }
         }
       }
     }
@@ -311,9 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     regs_dec<kRegsOther>();
     if (elect_one()) {
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, 22) && mbar_wait(&q_full[0], 0, abort_flag, p.status, 23);
-      auto issue_s_dp = [&](int it, bool s_part) {
-        const int st = it % C::STAGES;
+      // S^T or dP^T of the query tile at ring position gpos.
+      auto issue_s_dp = [&](int gpos, bool s_part) {
+        const int st = gpos % C::STAGES;
         if (s_part) {
           const uint32_t qb = sQ + st * C::QT_BYTES;
 #pragma unroll
@@ -330,56 +401,72 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_commit(dp_full);
         }
       };
-      if (ok) {
+      int g0 = 0;  // query-tile iterations of earlier items (ring positions, phases)
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        ItemRec e;
+        if (!(ok = take_item(k, e, true)) || e.L < 0) break;
+        const Walk w = walk(e);
+        ok = mbar_wait(kv_full, k & 1, abort_flag, p.status, 22) &&
+             mbar_wait(&q_full[g0 % C::STAGES], (g0 / C::STAGES) & 1, abort_flag, p.status, 23);
+        if (!ok) break;
         tc_fence_after();
-        issue_s_dp(0, true);
-        issue_s_dp(0, false);
-      }
-      for (int it = 0; ok && it < n_all; ++it) {
-        const int st = it % C::STAGES;
-        const uint32_t qb = sQ + st * C::QT_BYTES, ob = sDO + st * C::QT_BYTES;
-        // dV += P^T dO_i
-        if (!(ok = mbar_wait(p_full, it & 1, abort_flag, p.status, 24))) break;
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk)
-          umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + packed_col<BQ>(kk), mnmaj<D>(ob, BQ, kk),
-                      ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);  // A = P^T from TMEM
-        umma_commit(p_free);
-        // S^T for the next query tile overlaps the softmax warps' dS work.
-        const bool more = it + 1 < n_all;
-        if (more) {
-          const int st1 = (it + 1) % C::STAGES;
-          if (!(ok = mbar_wait(&q_full[st1], ((it + 1) / C::STAGES) & 1, abort_flag, p.status, 25))) break;
+        issue_s_dp(g0, true);
+        issue_s_dp(g0, false);
+        for (int it = 0; ok && it < w.n_all; ++it) {
+          const int gi = g0 + it;
+          const int st = gi % C::STAGES;
+          const uint32_t qb = sQ + st * C::QT_BYTES, ob = sDO + st * C::QT_BYTES;
+          // dV += P^T dO_i; the item's first dV / dK overwrite the accumulators
+          // once the previous item's epilogue has read them.
+          if (!(ok = mbar_wait(p_full, gi & 1, abort_flag, p.status, 24))) break;
+          if (it == 0 && k > 0 && !(ok = mbar_wait(acc_empty, (k - 1) & 1, abort_flag, p.status, 37)))
+            break;
           tc_fence_after();
-          issue_s_dp(it + 1, true);
-        }
-        // dS_i published (in TMEM over dP^T_i's columns and in smem).  dK first:
-        // it reads dS^T from those TMEM columns, so dP_{i+1} (which overwrites
-        // them) is issued after it; the dQ GEMM follows.
-        if (!(ok = mbar_wait(ds_full, it & 1, abort_flag, p.status, 26))) break;
-        tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk)
-          umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + packed_col<BQ>(kk), mnmaj<D>(qb, BQ, kk),
-                      ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);
-        if (more) issue_s_dp(it + 1, false);
-        if (it > 0 && !(ok = mbar_wait(dq_empty, (it - 1) & 1, abort_flag, p.status, 27))) break;
-        tc_fence_after();
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + packed_col<BQ>(kk), mnmaj<D>(ob, BQ, kk),
+                        ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);  // A = P^T from TMEM
+          umma_commit(p_free);
+          // S^T for the next query tile overlaps the softmax warps' dS work.
+          const bool more = it + 1 < w.n_all;
+          if (more) {
+            const int st1 = (gi + 1) % C::STAGES;
+            if (!(ok = mbar_wait(&q_full[st1], ((gi + 1) / C::STAGES) & 1, abort_flag, p.status, 25)))
+              break;
+            tc_fence_after();
+            issue_s_dp(gi + 1, true);
+          }
+          // dS_i published (in TMEM over dP^T_i's columns and in smem).  dK first:
+          // it reads dS^T from those TMEM columns, so dP_{i+1} (which overwrites
+          // them) is issued after it; the dQ GEMM follows.
+          if (!(ok = mbar_wait(ds_full, gi & 1, abort_flag, p.status, 26))) break;
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          if (C::DQT)  // dQ^T = K^T dS^T : A = K (MN-major, M = D), B = dS^T (MN-major, N = q)
-            umma_f16_ss(tmem + C::COL_DQ, mnmaj<D>(sK, BN, kk), pt_mnmaj(sDS, kk), ID_DQ,
-                        kk > 0 ? 1u : 0u);
-          else         // dQ = dS K : A = dS (MN-major, M = q), B = K (MN-major, N = D)
-            umma_f16_ss(tmem + C::COL_DQ, pt_mnmaj(sDS, kk), mnmaj<D>(sK, BN, kk), ID_DQ,
-                        kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < BQ / 16; ++kk)
+            umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + packed_col<BQ>(kk), mnmaj<D>(qb, BQ, kk),
+                        ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);
+          if (more) issue_s_dp(gi + 1, false);
+          if (gi > 0 && !(ok = mbar_wait(dq_empty, (gi - 1) & 1, abort_flag, p.status, 27))) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            if (C::DQT)  // dQ^T = K^T dS^T : A = K (MN-major, M = D), B = dS^T (MN-major, N = q)
+              umma_f16_ss(tmem + C::COL_DQ, mnmaj<D>(sK, BN, kk), pt_mnmaj(sDS, kk), ID_DQ,
+                          kk > 0 ? 1u : 0u);
+            else         // dQ = dS K : A = dS (MN-major, M = q), B = K (MN-major, N = D)
+              umma_f16_ss(tmem + C::COL_DQ, pt_mnmaj(sDS, kk), mnmaj<D>(sK, BN, kk), ID_DQ,
+                          kk > 0 ? 1u : 0u);
+          }
+          umma_commit(dq_full);
+          umma_commit(ds_free);
+          umma_commit(&q_empty[st]);
         }
-        umma_commit(dq_full);
-        umma_commit(ds_free);
-        umma_commit(&q_empty[st]);
+        if (!ok) break;
+        umma_commit(acc_done);
+        umma_commit(kv_empty);  // K, V may be replaced by the next item's
+        g0 += w.n_all;
       }
-      umma_commit(acc_done);
     }
   } else if (warp == 10 || warp == 11) {
     regs_dec<kRegsOther>();  // idle: only completes warpgroup 2's register release
@@ -389,32 +476,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int QH = BQ / 2;                // query columns per warp half
     const int hf = warp >> 2;                 // which half of the tile's queries
     const int kr = (warp & 3) * 32 + (threadIdx.x & 31);  // key row == TMEM lane
-    const int kidx = k0 + kr;
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    const bool key_ok = kidx < L;
     const float sl2 = p.scale_log2;
     const int t256 = threadIdx.x;             // 0..255 over both warpgroups
     bool ok = true;
+    int g0 = 0;  // query-tile iterations of earlier items (barrier phases)
+    for (int k = 0; ok; ++k) {
+    ItemRec e;
+    ok = __all_sync(0xffffffff, take_item(k, e, false));  // released after the epilogue
+    if (!ok || e.L < 0) break;
+    const Walk w = walk(e);
+    const int L = e.L, k0 = e.k0;
+    const int kidx = k0 + kr;
+    const bool key_ok = kidx < L;
     // LSE / Delta of query tile `it` staged as [BQ lse][BQ delta] (queries past L
     // read as 0; masked below), fetched one tile ahead.
     auto fetch = [&](int it_) -> float {
       if (t256 >= 2 * BQ) return 0.f;
-      const int q = q_tile(it_) * BQ + (t256 % BQ);
-      const int64_t base = (int64_t)q_head(it_) * p.T + row0 + q;
+      const int q = q_tile(w, it_) * BQ + (t256 % BQ);
+      const int64_t base = (int64_t)q_head(e, w, it_) * p.T + e.row0 + q;
       return q < L ? (t256 < BQ ? p.lse2T[base] : p.deltaT[base]) : 0.f;
     };
     float pre = fetch(0);
-    for (int it = 0; it < n_all; ++it) {
-      const int q0 = q_tile(it) * BQ;
+    for (int it = 0; it < w.n_all; ++it) {
+      const int gi = g0 + it;
+      const int q0 = q_tile(w, it) * BQ;
       const int qh0 = q0 + hf * QH;           // first query of this half
-      float* lse_s = lds + (it & 1) * 2 * BQ + hf * QH;
-      float* del_s = lds + (it & 1) * 2 * BQ + BQ + hf * QH;
-      if (t256 < 2 * BQ) lds[(it & 1) * 2 * BQ + t256] = pre;
-      if (it + 1 < n_all) pre = fetch(it + 1);
+      float* lse_s = lds + (gi & 1) * 2 * BQ + hf * QH;
+      float* del_s = lds + (gi & 1) * 2 * BQ + BQ + hf * QH;
+      if (t256 < 2 * BQ) lds[(gi & 1) * 2 * BQ + t256] = pre;
+      if (it + 1 < w.n_all) pre = fetch(it + 1);
       softmax_group_sync();
       const bool need_mask = (q0 + BQ > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
       // ---- P^T (this half's QH queries) from S^T
-      ok = mbar_wait(s_full, it & 1, abort_flag, p.status, 28);
+      ok = mbar_wait(s_full, gi & 1, abort_flag, p.status, 28);
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
       float pr[QH];
@@ -442,8 +537,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         pk[c4 * 2] = Pk2b<T>::pack(pr[c4 * 4], pr[c4 * 4 + 1]);
         pk[c4 * 2 + 1] = Pk2b<T>::pack(pr[c4 * 4 + 2], pr[c4 * 4 + 3]);
       }
-      if (it > 0) {  // dV_{i-1} read P^T_{i-1} from these columns
-        ok = mbar_wait(p_free, (it - 1) & 1, abort_flag, p.status, 29);
+      if (gi > 0) {  // dV_{i-1} read P^T_{i-1} from these columns
+        ok = mbar_wait(p_free, (gi - 1) & 1, abort_flag, p.status, 29);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       }
       // P^T (16-bit, two per column) over the first QH/2 of the QH fp32 columns
@@ -454,7 +549,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full);
       // ---- dS^T = P^T * (dP^T - Delta)
-      ok = mbar_wait(dp_full, it & 1, abort_flag, p.status, 30);
+      ok = mbar_wait(dp_full, gi & 1, abort_flag, p.status, 30);
       if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
@@ -473,8 +568,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 #pragma unroll
       for (int c = 0; c < QH / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
-      if (it > 0) {
-        ok = mbar_wait(ds_free, (it - 1) & 1, abort_flag, p.status, 31);
+      if (gi > 0) {
+        ok = mbar_wait(ds_free, (gi - 1) & 1, abort_flag, p.status, 31);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       }
       // dS^T: into TMEM over dP^T's first columns (A operand of dK) and into
@@ -488,11 +583,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // ---- dK, dV epilogue: 32-column chunk c belongs to half c % 2
     if (ok) {
-      ok = mbar_wait(acc_done, 0, abort_flag, p.status, 32);
+      ok = mbar_wait(acc_done, k & 1, abort_flag, p.status, 32);
       ok = __all_sync(0xffffffff, ok);
     }
     if (ok) {
       tc_fence_after();
+      // The record is still held in the ring: re-read where the rows go.
+      const ItemRec& er = item_ring[k % kItemRing];
+      const int64_t row0 = er.row0;
+      const int h = er.h;
       T* dvrow = reinterpret_cast<T*>(p.dv) + ((row0 + kidx) * p.Hkv + h) * D;
       T* dkrow = reinterpret_cast<T*>(p.dk) + ((row0 + kidx) * p.Hkv + h) * D;
 #pragma unroll
@@ -519,6 +618,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      tc_fence_before();
+      mbar_arrive(acc_empty);  // dV, dK are read: the next item may overwrite them
+    }
+    if (ok) mbar_arrive(&item_empty[k % kItemRing]);
+    g0 += w.n_all;
     }
   } else {
     // ------------------------------------------------------------ dQ reduction warps 12-15
@@ -526,11 +630,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ln = threadIdx.x - 384;  // TMEM lane: feature d (DQT) or query row
     const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
     const float sc = p.scale;
-    for (int it = 0; it < n_all; ++it) {
-      const int q0 = q_tile(it) * BQ;
-      const int hq = q_head(it);
-      bool ok = mbar_wait(dq_full, it & 1, abort_flag, p.status, 33);
-      if (!__all_sync(0xffffffff, ok)) break;
+    int g0 = 0;  // query-tile iterations of earlier items (barrier phases)
+    bool ok = true;
+    for (int k = 0; ok; ++k) {
+    ItemRec e;
+    ok = __all_sync(0xffffffff, take_item(k, e, true));
+    if (!ok || e.L < 0) break;
+    const Walk w = walk(e);
+    const int64_t row0 = e.row0;
+    const int L = e.L;
+    for (int it = 0; it < w.n_all; ++it) {
+      const int gi = g0 + it;
+      const int q0 = q_tile(w, it) * BQ;
+      const int hq = q_head(e, w, it);
+      ok = mbar_wait(dq_full, gi & 1, abort_flag, p.status, 33);
+      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
       tc_fence_after();
       if (C::DQT) {
         float v[BQ];
@@ -544,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Stage the scaled dQ tile as [BQ][D] fp32 and add it into dq_acc with one
         // TMA reduce.  Queries >= L carry exact zeros (their dS is 0), so adding
         // the whole box is safe even where it overlaps the next sequence.
-        if (ln == 0 && it > 0) bulk_wait_read_all();
+        if (ln == 0 && gi > 0) bulk_wait_read_all();
         dq_group_sync();
         float* sdq = reinterpret_cast<float*>(smem + C::OFF_DQ);
 #pragma unroll
@@ -575,6 +689,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(dq_empty);
       }
     }
+    g0 += w.n_all;
+    }
     if (C::DQT && ln == 0) bulk_wait_all();  // smem must outlive the reduces
   }
 
@@ -584,7 +700,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #ifdef SCREE_TRACE
   if (threadIdx.x == 0) {
     scree_trace_sm[62] += (unsigned long long)(clock64() - t_cta0);
-    scree_trace_sm[63] += (unsigned long long)(n_all);
   }
   __syncthreads();
   if (threadIdx.x < 64) atomicAdd(&g_bwd_trace[threadIdx.x], scree_trace_sm[threadIdx.x]);
@@ -727,11 +842,9 @@ int run_bwd_typed(const void* dout, const void* q, const void* k, const void* v,
   p.dq_acc = dq_acc;
   p.dk = dk;
   p.dv = dv;
-  const int64_t grid = max_tiles(B, Tn, BN) * Hkv;
-  if (grid >= (1ll << 31)) {
-    set_last_error("attn_bwd: grid too large");
-    return SCREE_ERR_INVALID;
-  }
+  // Persistent CTAs, one per SM (each holds all 512 TMEM columns); the items
+  // themselves are counted on the device.
+  const int64_t grid = std::min<int64_t>(max_tiles(B, Tn, BN) * Hkv, (int64_t)num_sms());
 #define SCREE_BWD_CASE(DD)                                                        \
   if (D == DD) {                                                                  \
     if (p.G > 1)                                                                  \
