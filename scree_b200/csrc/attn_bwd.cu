@@ -8,8 +8,10 @@
 //   dK = scale * dS^T Q,    dQ = scale * dS K
 // Five GEMMs per (key tile, query tile) pair, none recomputed.
 //
-// One CTA owns a 128-key tile of one head (K, V resident in shared memory) and
-// loops over the sequence's query tiles of BQ rows:
+// A work item is a 128-key tile of one K/V head (K, V resident in shared
+// memory); the kernel is persistent (one CTA per SM takes items in schedule
+// order from a device counter) and, per item, loops over the sequence's query
+// tiles of BQ rows:
 //   warp 8    TMA: K, V once; Q_i, dO_i into a ring
 //   warp 9    MMA: S^T = K Q_i^T, dP^T = V dO_i^T, dV += P^T dO_i,
 //                  dK += dS^T Q_i, dQ_i (see below)

@@ -14,7 +14,7 @@ namespace scree {
 //   sequences in descending length (cost ~ L^2; longest first = LPT order),
 //   then head-major within a sequence, then the sequence's tiles, heaviest first
 //   (forward causal: the last query tile; backward causal: the first key tile).
-// A block index maps to its item by a binary search over SeqRef::item_start.
+// An item index maps to its item by a binary search over SeqRef::item_start.
 struct SeqRef {
   int32_t seq;         // index into offsets
   int32_t ntiles;      // tiles of `outer` rows in this sequence

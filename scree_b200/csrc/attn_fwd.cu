@@ -4,10 +4,12 @@
 //   S = Q K^T * scale, causal mask k > q -> -inf, P = softmax(S), O = P V,
 //   LSE = m + ln(l)  (natural log; triton/varlen_attention.py:160)
 //
-// One CTA owns 256 query rows of one head as two 128-row tiles, A and B, that
+// A work item is 256 query rows of one head as two 128-row tiles, A and B, that
 // share every 128-key K/V tile the sequence streams through shared memory, so
-// each K/V byte feeds twice the tensor work of a single-tile CTA (the L2 -> SM
-// feed of K/V is what limits a 128-row CTA).
+// each K/V byte feeds twice the tensor work of a single-tile item (the L2 -> SM
+// feed of K/V is what limits a 128-row tile).  The kernel is persistent: one
+// CTA per SM takes items in schedule order from a device counter, and the
+// rings and barrier phases below run on across its items.
 //
 //   warp 8  (TMA)  lane 0: Q_A, Q_B once, then the K ring; lane 1: the V ring
 //   warp 9  (MMA)  one thread issues tcgen05.mma: S_X = Q_X K_j^T (X = A, B) and
