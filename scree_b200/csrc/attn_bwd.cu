@@ -484,147 +484,147 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int g0 = 0;  // query-tile iterations of earlier items (barrier phases)
     for (int k = 0; ok; ++k) {
-    ItemRec e;
-    ok = __all_sync(0xffffffff, take_item(k, e, false));  // released after the epilogue
-    if (!ok || e.L < 0) break;
-    const Walk w = walk(e);
-    const int L = e.L, k0 = e.k0;
-    const int kidx = k0 + kr;
-    const bool key_ok = kidx < L;
-    // LSE / Delta of query tile `it` staged as [BQ lse][BQ delta] (queries past L
-    // read as 0; masked below), fetched one tile ahead.
-    auto fetch = [&](int it_) -> float {
-      if (t256 >= 2 * BQ) return 0.f;
-      const int q = q_tile(w, it_) * BQ + (t256 % BQ);
-      const int64_t base = (int64_t)q_head(e, w, it_) * p.T + e.row0 + q;
-      return q < L ? (t256 < BQ ? p.lse2T[base] : p.deltaT[base]) : 0.f;
-    };
-    float pre = fetch(0);
-    for (int it = 0; it < w.n_all; ++it) {
-      const int gi = g0 + it;
-      const int q0 = q_tile(w, it) * BQ;
-      const int qh0 = q0 + hf * QH;           // first query of this half
-      float* lse_s = lds + (gi & 1) * 2 * BQ + hf * QH;
-      float* del_s = lds + (gi & 1) * 2 * BQ + BQ + hf * QH;
-      if (t256 < 2 * BQ) lds[(gi & 1) * 2 * BQ + t256] = pre;
-      if (it + 1 < w.n_all) pre = fetch(it + 1);
-      softmax_group_sync();
-      const bool need_mask = (q0 + BQ > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
-      // ---- P^T (this half's QH queries) from S^T
-      ok = mbar_wait(s_full, gi & 1, abort_flag, p.status, 28);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      tc_fence_after();
-      float pr[QH];
-#pragma unroll
-      for (int c = 0; c < QH / 32; ++c)
-        tmem_ld32(lane_base + C::COL_S + hf * QH + c * 32,
-                  *reinterpret_cast<float(*)[32]>(&pr[c * 32]));
-      tmem_wait_ld();
-      uint32_t pk[QH / 2];
-#pragma unroll
-      for (int c4 = 0; c4 < QH / 4; ++c4) {
-        const float4 l4 = reinterpret_cast<const float4*>(lse_s)[c4];  // one LDS.128
-        const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int c = c4 * 4 + e;
-          float xv = ex2_approx(fmaf(pr[c], sl2, -lv[e]));
-          if (need_mask) {
-            const int q = qh0 + c;
-            const bool valid = key_ok && q < L && (!CAUSAL || q >= kidx);
-            xv = valid ? xv : 0.f;
-          }
-          pr[c] = xv;
-        }
-        pk[c4 * 2] = Pk2b<T>::pack(pr[c4 * 4], pr[c4 * 4 + 1]);
-        pk[c4 * 2 + 1] = Pk2b<T>::pack(pr[c4 * 4 + 2], pr[c4 * 4 + 3]);
-      }
-      if (gi > 0) {  // dV_{i-1} read P^T_{i-1} from these columns
-        ok = mbar_wait(p_free, (gi - 1) & 1, abort_flag, p.status, 29);
+      ItemRec e;
+      ok = __all_sync(0xffffffff, take_item(k, e, false));  // released after the epilogue
+      if (!ok || e.L < 0) break;
+      const Walk w = walk(e);
+      const int L = e.L, k0 = e.k0;
+      const int kidx = k0 + kr;
+      const bool key_ok = kidx < L;
+      // LSE / Delta of query tile `it` staged as [BQ lse][BQ delta] (queries past L
+      // read as 0; masked below), fetched one tile ahead.
+      auto fetch = [&](int it_) -> float {
+        if (t256 >= 2 * BQ) return 0.f;
+        const int q = q_tile(w, it_) * BQ + (t256 % BQ);
+        const int64_t base = (int64_t)q_head(e, w, it_) * p.T + e.row0 + q;
+        return q < L ? (t256 < BQ ? p.lse2T[base] : p.deltaT[base]) : 0.f;
+      };
+      float pre = fetch(0);
+      for (int it = 0; it < w.n_all; ++it) {
+        const int gi = g0 + it;
+        const int q0 = q_tile(w, it) * BQ;
+        const int qh0 = q0 + hf * QH;           // first query of this half
+        float* lse_s = lds + (gi & 1) * 2 * BQ + hf * QH;
+        float* del_s = lds + (gi & 1) * 2 * BQ + BQ + hf * QH;
+        if (t256 < 2 * BQ) lds[(gi & 1) * 2 * BQ + t256] = pre;
+        if (it + 1 < w.n_all) pre = fetch(it + 1);
+        softmax_group_sync();
+        const bool need_mask = (q0 + BQ > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
+        // ---- P^T (this half's QH queries) from S^T
+        ok = mbar_wait(s_full, gi & 1, abort_flag, p.status, 28);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      }
-      // P^T (16-bit, two per column) over the first QH/2 of the QH fp32 columns
-      // this half read: never over the other half's columns (warps w and w+4
-      // share TMEM lanes and do not wait for each other).
-      tmem_st_packed<QH / 2>(lane_base + C::COL_S + hf * QH, pk);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(p_full);
-      // ---- dS^T = P^T * (dP^T - Delta)
-      ok = mbar_wait(dp_full, gi & 1, abort_flag, p.status, 30);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      tc_fence_after();
+        tc_fence_after();
+        float pr[QH];
 #pragma unroll
-      for (int c = 0; c < QH / 32; ++c) {
-        float dp[32];
-        tmem_ld32(lane_base + C::COL_DP + hf * QH + c * 32, dp);
+        for (int c = 0; c < QH / 32; ++c)
+          tmem_ld32(lane_base + C::COL_S + hf * QH + c * 32,
+                    *reinterpret_cast<float(*)[32]>(&pr[c * 32]));
         tmem_wait_ld();
+        uint32_t pk[QH / 2];
 #pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
-          const float4 d4 = reinterpret_cast<const float4*>(del_s)[c * 8 + e4];
-          pr[c * 32 + e4 * 4 + 0] *= (dp[e4 * 4 + 0] - d4.x);
-          pr[c * 32 + e4 * 4 + 1] *= (dp[e4 * 4 + 1] - d4.y);
-          pr[c * 32 + e4 * 4 + 2] *= (dp[e4 * 4 + 2] - d4.z);
-          pr[c * 32 + e4 * 4 + 3] *= (dp[e4 * 4 + 3] - d4.w);
+        for (int c4 = 0; c4 < QH / 4; ++c4) {
+          const float4 l4 = reinterpret_cast<const float4*>(lse_s)[c4];  // one LDS.128
+          const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int c = c4 * 4 + e;
+            float xv = ex2_approx(fmaf(pr[c], sl2, -lv[e]));
+            if (need_mask) {
+              const int q = qh0 + c;
+              const bool valid = key_ok && q < L && (!CAUSAL || q >= kidx);
+              xv = valid ? xv : 0.f;
+            }
+            pr[c] = xv;
+          }
+          pk[c4 * 2] = Pk2b<T>::pack(pr[c4 * 4], pr[c4 * 4 + 1]);
+          pk[c4 * 2 + 1] = Pk2b<T>::pack(pr[c4 * 4 + 2], pr[c4 * 4 + 3]);
         }
-      }
-#pragma unroll
-      for (int c = 0; c < QH / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
-      if (gi > 0) {
-        ok = mbar_wait(ds_free, (gi - 1) & 1, abort_flag, p.status, 31);
+        if (gi > 0) {  // dV_{i-1} read P^T_{i-1} from these columns
+          ok = mbar_wait(p_free, (gi - 1) & 1, abort_flag, p.status, 29);
+          if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+        }
+        // P^T (16-bit, two per column) over the first QH/2 of the QH fp32 columns
+        // this half read: never over the other half's columns (warps w and w+4
+        // share TMEM lanes and do not wait for each other).
+        tmem_st_packed<QH / 2>(lane_base + C::COL_S + hf * QH, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(p_full);
+        // ---- dS^T = P^T * (dP^T - Delta)
+        ok = mbar_wait(dp_full, gi & 1, abort_flag, p.status, 30);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      }
-      // dS^T: into TMEM over dP^T's first columns (A operand of dK) and into
-      // smem (B operand of the dQ GEMM).
-      tmem_st_packed<QH / 2>(lane_base + C::COL_DP + hf * QH, pk);
-      write_row_sw128<T, QH>(smem + C::OFF_DS, kr, pr, hf * (QH / 8));
-      tmem_wait_st();
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(ds_full);
-    }
-    // ---- dK, dV epilogue: 32-column chunk c belongs to half c % 2
-    if (ok) {
-      ok = mbar_wait(acc_done, k & 1, abort_flag, p.status, 32);
-      ok = __all_sync(0xffffffff, ok);
-    }
-    if (ok) {
-      tc_fence_after();
-      // The record is still held in the ring: re-read where the rows go.
-      const ItemRec& er = item_ring[k % kItemRing];
-      const int64_t row0 = er.row0;
-      const int h = er.h;
-      T* dvrow = reinterpret_cast<T*>(p.dv) + ((row0 + kidx) * p.Hkv + h) * D;
-      T* dkrow = reinterpret_cast<T*>(p.dk) + ((row0 + kidx) * p.Hkv + h) * D;
+        tc_fence_after();
 #pragma unroll
-      for (int pass = 0; pass < 2; ++pass) {
-        const int col = pass == 0 ? C::COL_DV : C::COL_DK;
-        const float mul = pass == 0 ? 1.f : p.scale;
-        T* dst = pass == 0 ? dvrow : dkrow;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          if ((c & 1) != hf) continue;
-          float v[32];
-          tmem_ld32(lane_base + col + c * 32, v);
+        for (int c = 0; c < QH / 32; ++c) {
+          float dp[32];
+          tmem_ld32(lane_base + C::COL_DP + hf * QH + c * 32, dp);
           tmem_wait_ld();
-          if (key_ok) {
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-              uint4 w;
-              w.x = Pk2b<T>::pack(v[u * 8 + 0] * mul, v[u * 8 + 1] * mul);
-              w.y = Pk2b<T>::pack(v[u * 8 + 2] * mul, v[u * 8 + 3] * mul);
-              w.z = Pk2b<T>::pack(v[u * 8 + 4] * mul, v[u * 8 + 5] * mul);
-              w.w = Pk2b<T>::pack(v[u * 8 + 6] * mul, v[u * 8 + 7] * mul);
-              *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = w;
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 d4 = reinterpret_cast<const float4*>(del_s)[c * 8 + e4];
+            pr[c * 32 + e4 * 4 + 0] *= (dp[e4 * 4 + 0] - d4.x);
+            pr[c * 32 + e4 * 4 + 1] *= (dp[e4 * 4 + 1] - d4.y);
+            pr[c * 32 + e4 * 4 + 2] *= (dp[e4 * 4 + 2] - d4.z);
+            pr[c * 32 + e4 * 4 + 3] *= (dp[e4 * 4 + 3] - d4.w);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < QH / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
+        if (gi > 0) {
+          ok = mbar_wait(ds_free, (gi - 1) & 1, abort_flag, p.status, 31);
+          if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+        }
+        // dS^T: into TMEM over dP^T's first columns (A operand of dK) and into
+        // smem (B operand of the dQ GEMM).
+        tmem_st_packed<QH / 2>(lane_base + C::COL_DP + hf * QH, pk);
+        write_row_sw128<T, QH>(smem + C::OFF_DS, kr, pr, hf * (QH / 8));
+        tmem_wait_st();
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(ds_full);
+      }
+      // ---- dK, dV epilogue: 32-column chunk c belongs to half c % 2
+      if (ok) {
+        ok = mbar_wait(acc_done, k & 1, abort_flag, p.status, 32);
+        ok = __all_sync(0xffffffff, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+        // The record is still held in the ring: re-read where the rows go.
+        const ItemRec& er = item_ring[k % kItemRing];
+        const int64_t row0 = er.row0;
+        const int h = er.h;
+        T* dvrow = reinterpret_cast<T*>(p.dv) + ((row0 + kidx) * p.Hkv + h) * D;
+        T* dkrow = reinterpret_cast<T*>(p.dk) + ((row0 + kidx) * p.Hkv + h) * D;
+#pragma unroll
+        for (int pass = 0; pass < 2; ++pass) {
+          const int col = pass == 0 ? C::COL_DV : C::COL_DK;
+          const float mul = pass == 0 ? 1.f : p.scale;
+          T* dst = pass == 0 ? dvrow : dkrow;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            if ((c & 1) != hf) continue;
+            float v[32];
+            tmem_ld32(lane_base + col + c * 32, v);
+            tmem_wait_ld();
+            if (key_ok) {
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                uint4 w;
+                w.x = Pk2b<T>::pack(v[u * 8 + 0] * mul, v[u * 8 + 1] * mul);
+                w.y = Pk2b<T>::pack(v[u * 8 + 2] * mul, v[u * 8 + 3] * mul);
+                w.z = Pk2b<T>::pack(v[u * 8 + 4] * mul, v[u * 8 + 5] * mul);
+                w.w = Pk2b<T>::pack(v[u * 8 + 6] * mul, v[u * 8 + 7] * mul);
+                *reinterpret_cast<uint4*>(dst + c * 32 + u * 8) = w;
+              }
             }
           }
         }
+        tc_fence_before();
+        mbar_arrive(acc_empty);  // dV, dK are read: the next item may overwrite them
       }
-      tc_fence_before();
-      mbar_arrive(acc_empty);  // dV, dK are read: the next item may overwrite them
-    }
-    if (ok) mbar_arrive(&item_empty[k % kItemRing]);
-    g0 += w.n_all;
+      if (ok) mbar_arrive(&item_empty[k % kItemRing]);
+      g0 += w.n_all;
     }
   } else {
     // ------------------------------------------------------------ dQ reduction warps 12-15
@@ -635,63 +635,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g0 = 0;  // query-tile iterations of earlier items (barrier phases)
     bool ok = true;
     for (int k = 0; ok; ++k) {
-    ItemRec e;
-    ok = __all_sync(0xffffffff, take_item(k, e, true));
-    if (!ok || e.L < 0) break;
-    const Walk w = walk(e);
-    const int64_t row0 = e.row0;
-    const int L = e.L;
-    for (int it = 0; it < w.n_all; ++it) {
-      const int gi = g0 + it;
-      const int q0 = q_tile(w, it) * BQ;
-      const int hq = q_head(e, w, it);
-      ok = mbar_wait(dq_full, gi & 1, abort_flag, p.status, 33);
-      if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
-      tc_fence_after();
-      if (C::DQT) {
-        float v[BQ];
+      ItemRec e;
+      ok = __all_sync(0xffffffff, take_item(k, e, true));
+      if (!ok || e.L < 0) break;
+      const Walk w = walk(e);
+      const int64_t row0 = e.row0;
+      const int L = e.L;
+      for (int it = 0; it < w.n_all; ++it) {
+        const int gi = g0 + it;
+        const int q0 = q_tile(w, it) * BQ;
+        const int hq = q_head(e, w, it);
+        ok = mbar_wait(dq_full, gi & 1, abort_flag, p.status, 33);
+        if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+        tc_fence_after();
+        if (C::DQT) {
+          float v[BQ];
 #pragma unroll
-        for (int c = 0; c < BQ / 32; ++c)
-          tmem_ld32(lane_base + C::COL_DQ + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(dq_empty);
-        {
-        // Stage the scaled dQ tile as [BQ][D] fp32 and add it into dq_acc with one
-        // TMA reduce.  Queries >= L carry exact zeros (their dS is 0), so adding
-        // the whole box is safe even where it overlaps the next sequence.
-        if (ln == 0 && gi > 0) bulk_wait_read_all();
-        dq_group_sync();
-        float* sdq = reinterpret_cast<float*>(smem + C::OFF_DQ);
-#pragma unroll
-        for (int c = 0; c < BQ; ++c) sdq[c * D + ln] = v[c] * sc;
-        fence_proxy_async_smem();
-        dq_group_sync();
-        if (ln == 0) {
-          tma_reduce_add_3d(&tm_dq, sdq, 0, hq, (int)(row0 + q0));
-          bulk_commit();
-        }
-        }
-      } else {
-        const int q = q0 + ln;
-        float* base = p.dq_acc + ((row0 + q) * p.H + hq) * D;
-#pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          float v[32];
-          tmem_ld32(lane_base + C::COL_DQ + c * 32, v);
+          for (int c = 0; c < BQ / 32; ++c)
+            tmem_ld32(lane_base + C::COL_DQ + c * 32, *reinterpret_cast<float(*)[32]>(&v[c * 32]));
           tmem_wait_ld();
-          if (q < L) {
+          tc_fence_before();
+          mbar_arrive(dq_empty);
+          {
+          // Stage the scaled dQ tile as [BQ][D] fp32 and add it into dq_acc with one
+          // TMA reduce.  Queries >= L carry exact zeros (their dS is 0), so adding
+          // the whole box is safe even where it overlaps the next sequence.
+          if (ln == 0 && gi > 0) bulk_wait_read_all();
+          dq_group_sync();
+          float* sdq = reinterpret_cast<float*>(smem + C::OFF_DQ);
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
-              red_add_v4(base + c * 32 + u * 4, v[u * 4] * sc, v[u * 4 + 1] * sc,
-                         v[u * 4 + 2] * sc, v[u * 4 + 3] * sc);
+          for (int c = 0; c < BQ; ++c) sdq[c * D + ln] = v[c] * sc;
+          fence_proxy_async_smem();
+          dq_group_sync();
+          if (ln == 0) {
+            tma_reduce_add_3d(&tm_dq, sdq, 0, hq, (int)(row0 + q0));
+            bulk_commit();
           }
+          }
+        } else {
+          const int q = q0 + ln;
+          float* base = p.dq_acc + ((row0 + q) * p.H + hq) * D;
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            float v[32];
+            tmem_ld32(lane_base + C::COL_DQ + c * 32, v);
+            tmem_wait_ld();
+            if (q < L) {
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+                red_add_v4(base + c * 32 + u * 4, v[u * 4] * sc, v[u * 4 + 1] * sc,
+                           v[u * 4 + 2] * sc, v[u * 4 + 3] * sc);
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(dq_empty);
         }
-        tc_fence_before();
-        mbar_arrive(dq_empty);
       }
-    }
-    g0 += w.n_all;
+      g0 += w.n_all;
     }
     if (C::DQT && ln == 0) bulk_wait_all();  // smem must outlive the reduces
   }
