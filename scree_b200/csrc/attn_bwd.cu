@@ -11,18 +11,22 @@
 // A work item is a 128-key tile of one K/V head (K, V resident in shared
 // memory); the kernel is persistent (one CTA per SM takes items in schedule
 // order from a device counter) and, per item, loops over the sequence's query
-// tiles of BQ rows:
-//   warp 8    TMA: K, V once; Q_i, dO_i into a ring
-//   warp 9    MMA: S^T = K Q_i^T, dP^T = V dO_i^T, dV += P^T dO_i,
-//                  dK += dS^T Q_i, dQ_i (see below)
-//   warps 0-3 thread = key row = TMEM lane: P^T, dS^T from S^T, dP^T
-//   warps 4-7 read dQ_i from TMEM and add it into an fp32 accumulator in global
-//             memory with vector reductions; a final kernel casts it to q's dtype.
+// tiles of BQ rows.  Warps, in launch order:
+//   4 NP P/dS warps  thread = key row = TMEM lane: P^T, dS^T from S^T, dP^T; the
+//                    NP warps of one lane quadrant each take BQ / NP query columns
+//                    (NP = 4 at D = 128: 768 threads; NP = 2 below: 512 threads)
+//   TMA warp         K, V once; Q_i, dO_i into a ring
+//   MMA warp         S^T = K Q_i^T, dP^T = V dO_i^T, dV += P^T dO_i,
+//                    dK += dS^T Q_i, dQ_i (see below)
+//   two idle warps, then 4 dQ warps: read dQ_i from TMEM and add it into an fp32
+//                    accumulator in global memory; a final kernel casts it to q's dtype.
 // Two shapes:
 //   D = 128: BQ = 64 and dQ_i^T = K^T dS^T (M = D = 128 lanes, N = 64 queries),
-//            so each warp's reductions cover 32 consecutive features (128 B);
-//   D <= 64: BQ = 128 and dQ_i = dS K (M = 128 queries, N = D).
-// TMEM columns: S^T [0,BQ), dP^T [BQ,2BQ), dV [2BQ,2BQ+D), dK [.., +D), dQ [.., +BQ or D).
+//            staged in shared memory and added with one TMA reduce per tile;
+//   D <= 64: BQ = 128 and dQ_i = dS K (M = 128 queries, N = D), vector reductions.
+// TMEM columns: S^T [0,BQ), dP^T [BQ,2BQ), dV [2BQ,2BQ+D), dK [.., +D), dQ [.., +BQ or D),
+// and where the 512 columns allow it (D = 128, D = 32) a second S^T buffer after dQ:
+// S^T of tile i + 2 is then issued right after dP^T of tile i + 1.
 #include <algorithm>
 #ifdef SCREE_TRACE
 // Profiling build only: per-site wait cycles (lane 0 of each waiting warp),
@@ -33,35 +37,61 @@ static __device__ unsigned long long g_bwd_trace[64];
 static __shared__ unsigned long long scree_trace_sm[64];  // per-CTA, flushed at exit
 #endif
 #include "attn_common.cuh"
+#ifdef SCREE_TRACE
+#define SW_MARK(site)                          \
+  do {                                         \
+    const long long t_ = clock64();            \
+    SCREE_TRACE_ADD(site, t_ - t_mark);        \
+    t_mark = t_;                               \
+  } while (0)
+#else
+#define SW_MARK(site) \
+  do {                \
+  } while (0)
+#endif
 
 namespace scree {
 namespace {
 
 constexpr int BN = 128;  // keys per CTA
-// Warpgroups 0-1: P^T / dS^T warps (warps w and w+4 share TMEM lanes 32(w%4)..,
-// each takes half of a tile's query columns); warpgroup 2: TMA warp, MMA warp,
-// two idle warps; warpgroup 3: dQ reduction warps.  Launched at 128 registers per
-// thread (65,536 / 512); the P/dS warpgroups grow to 152, warpgroup 2 shrinks to
-// 80 and warpgroup 3 to 120: 256 x 152 + 128 x 80 + 128 x 120 = 64,512 <= 65,536.
-constexpr int kThreads = 512;
-
-
+// Roles: NP P^T / dS^T warpgroups first (the NP warps w % 4 == j share TMEM lanes
+// 32j..32j+31, each takes 1/NP of a tile's query columns), then one warpgroup of
+// TMA warp, MMA warp and two idle warps, then the four dQ reduction warps.
+//   NP = 2 (D <= 64): 512 threads launched at 128 registers; the P/dS warpgroups
+//     grow to 152, warpgroup 2 shrinks to 80 and the dQ warps to 120:
+//     256 x 152 + 128 x 80 + 128 x 120 = 64,512 <= 65,536.
+//   NP = 4 (D = 128, 16 query columns per P/dS thread): 768 threads at the
+//     launch's register count (at most 80), no reallocation.
 constexpr int kRegsSoftmax = 152, kRegsOther = 80, kRegsDq = 120;
 // Item records reach the roles through a ring: the TMA thread takes the next
-// item from the schedule's counter and publishes it; the MMA thread, the 256
-// P/dS threads and the 128 dQ threads read it.
+// item from the schedule's counter and publishes it; the MMA thread, the P/dS
+// threads and the 128 dQ threads read it.
 constexpr int kItemRing = 4;
-constexpr int kItemConsumers = 1 + 256 + 128;
 
 template <int D>
 struct BwdCfg {
   static constexpr bool DQT = (D == 128);
   static constexpr int BQ = DQT ? 64 : 128;
+  // NP P/dS warps per TMEM lane quadrant, each taking BQ / NP query columns.
+  static constexpr int NP = D == 128 ? 4 : 2;
+  static constexpr int QH = BQ / NP;          // query columns per P/dS thread
+  static constexpr int SWT = NP * 128;        // P/dS threads
+  static constexpr int THREADS = SWT + 256;
+  static constexpr int ITEM_CONSUMERS = 1 + SWT + 128;
   static constexpr int SWB = D >= 64 ? 128 : 64;
   static constexpr int CHUNK = SWB / 2;
   static constexpr int NCHUNK = D / CHUNK;
   static constexpr uint32_t SWZ = SWB == 128 ? SW_128B : SW_64B;
-  static constexpr int STAGES = 2;
+  // S^T double-buffered in TMEM where the columns allow it (D = 128, D = 32): S^T
+  // of tile i + 2 is computed while the P/dS warps work on tile i + 1, so they
+  // never wait for it; a third Q / dO stage keeps its load ahead of that MMA.
+  static constexpr int COL_S1 = 2 * BQ + 2 * D + (DQT ? BQ : D);
+#ifdef SCREE_BWD_NO_SDB
+  static constexpr bool SDB = false;
+#else
+  static constexpr bool SDB = COL_S1 + BQ <= 512;
+#endif
+  static constexpr int STAGES = SDB ? 3 : 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int QT_BYTES = BQ * D * 2;
   static constexpr int PT_BYTES = BN * BQ * 2;
@@ -138,13 +168,13 @@ template <> struct Pk2b<__half> {
   }
 };
 
-// TMEM column of k-step kk (16 queries) of a packed P^T / dS^T tile.  Each half
-// of the tile's queries is packed into the first half of its own fp32 columns:
-// queries [0, BQ/2) at columns [0, BQ/4), queries [BQ/2, BQ) at [BQ/2, 3BQ/4).
-template <int BQ>
+// TMEM column of k-step kk (16 queries) of a packed P^T / dS^T tile.  Each of
+// the NP parts of the tile's queries is packed into the first half of its own
+// fp32 columns: queries [j QH, (j + 1) QH) at columns [j QH, j QH + QH / 2).
+template <int BQ, int NP>
 __device__ __forceinline__ uint32_t packed_col(int kk) {
-  constexpr int KH = BQ / 32;  // k-steps per half
-  return (uint32_t)((kk / KH) * (BQ / 2) + (kk % KH) * 8);
+  constexpr int KH = BQ / (16 * NP);  // k-steps per part
+  return (uint32_t)((kk / KH) * (BQ / NP) + (kk % KH) * 8);
 }
 
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
@@ -153,9 +183,10 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
-// Named barriers over the 256 P/dS threads (warps 0-7) and the 128 dQ threads.
+// Named barriers over the N P/dS threads (the first warps) and the 128 dQ threads.
+template <int N>
 __device__ __forceinline__ void softmax_group_sync() {
-  asm volatile("bar.sync 1, 256;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void dq_group_sync() {
   asm volatile("bar.sync 2, 128;" ::: "memory");
@@ -180,7 +211,7 @@ __device__ __forceinline__ void write_row_sw128(uint8_t* base, int kr, const flo
 }
 
 template <int D, typename T, bool CAUSAL, bool GQA>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(BwdCfg<D>::THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v,
@@ -263,8 +294,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* kv_full = bars + 0;
   uint64_t* q_full = bars + 1;               // [STAGES]
   uint64_t* q_empty = q_full + C::STAGES;    // [STAGES]
-  uint64_t* s_full = q_empty + C::STAGES;
-  uint64_t* dp_full = s_full + 1;
+  uint64_t* s_full = q_empty + C::STAGES;  // [2]: one per S^T buffer (SDB)
+  uint64_t* dp_full = s_full + 2;
   uint64_t* p_full = dp_full + 1;
   uint64_t* ds_full = p_full + 1;
   uint64_t* p_free = ds_full + 1;
@@ -294,26 +325,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
-    mbar_init(s_full, 1);
+    mbar_init(&s_full[0], 1);
+    mbar_init(&s_full[1], 1);
     mbar_init(dp_full, 1);
-    mbar_init(p_full, 256);
-    mbar_init(ds_full, 256);
+    mbar_init(p_full, C::SWT);
+    mbar_init(ds_full, C::SWT);
     mbar_init(p_free, 1);
     mbar_init(ds_free, 1);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(acc_done, 1);
-    mbar_init(acc_empty, 256);
+    mbar_init(acc_empty, C::SWT);
     mbar_init(kv_empty, 1);
     for (int k = 0; k < kItemRing; ++k) {
       mbar_init(&item_full[k], 1);
-      mbar_init(&item_empty[k], kItemConsumers);
+      mbar_init(&item_empty[k], C::ITEM_CONSUMERS);
     }
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 9) tmem_alloc<C::TMEM_COLS>(tmem_slot);
-  if (warp == 8 && (threadIdx.x & 31) == 0) {
+  constexpr int W_TMA = C::SWT / 32, W_MMA = W_TMA + 1, W_DQ = W_TMA + 4;
+  if (warp == W_MMA) tmem_alloc<C::TMEM_COLS>(tmem_slot);
+  if (warp == W_TMA && (threadIdx.x & 31) == 0) {
     tma_prefetch_desc(&tm_q);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
@@ -334,9 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     return true;
   };
 
-  if (warp == 8) {
+  if (warp == W_TMA) {
     // ------------------------------------------------------------ TMA producer
-    regs_dec<kRegsOther>();
+    if constexpr (C::NP == 2) regs_dec<kRegsOther>();
     if (elect_one()) {
       int gq = 0;  // Q / dO tiles loaded so far (ring position)
       bool ok = true;
@@ -380,20 +413,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == W_MMA) {
     // ------------------------------------------------------------ MMA issuer
-    regs_dec<kRegsOther>();
+    if constexpr (C::NP == 2) regs_dec<kRegsOther>();
     if (elect_one()) {
       // S^T or dP^T of the query tile at ring position gpos.
       auto issue_s_dp = [&](int gpos, bool s_part) {
         const int st = gpos % C::STAGES;
         if (s_part) {
           const uint32_t qb = sQ + st * C::QT_BYTES;
+          const uint32_t col = (C::SDB && (gpos & 1)) ? C::COL_S1 : C::COL_S;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk)
-            umma_f16_ss(tmem + C::COL_S, kmaj<D>(sK, BN, kk), kmaj<D>(qb, BQ, kk), ID_S,
+            umma_f16_ss(tmem + col, kmaj<D>(sK, BN, kk), kmaj<D>(qb, BQ, kk), ID_S,
                         kk > 0 ? 1u : 0u);
-          umma_commit(s_full);
+          umma_commit(&s_full[C::SDB ? (gpos & 1) : 0]);
         } else {
           const uint32_t ob = sDO + st * C::QT_BYTES;
 #pragma unroll
@@ -405,7 +439,75 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int g0 = 0;  // query-tile iterations of earlier items (ring positions, phases)
       bool ok = true;
-      for (int k = 0; ok; ++k) {
+      if constexpr (C::SDB) {
+        // Per tile i: dV_i, dK_i, dP_{i+1}, S_{i+2} (into tile i's S buffer, which
+        // dV_i was the last to read), dQ_i.  MMAs of one thread execute in issue
+        // order, so an MMA never overwrites TMEM that an earlier one still reads.
+        auto wait_q = [&](int gpos) {
+          return mbar_wait(&q_full[gpos % C::STAGES], (gpos / C::STAGES) & 1, abort_flag, p.status,
+                           25);
+        };
+        for (int k = 0; ok; ++k) {
+          ItemRec e;
+          if (!(ok = take_item(k, e, true)) || e.L < 0) break;
+          const Walk w = walk(e);
+          ok = mbar_wait(kv_full, k & 1, abort_flag, p.status, 22) && wait_q(g0);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s_dp(g0, true);
+          issue_s_dp(g0, false);
+          if (w.n_all > 1) {
+            if (!(ok = wait_q(g0 + 1))) break;
+            tc_fence_after();
+            issue_s_dp(g0 + 1, true);
+          }
+          for (int it = 0; ok && it < w.n_all; ++it) {
+            const int gi = g0 + it;
+            const int st = gi % C::STAGES;
+            const uint32_t qb = sQ + st * C::QT_BYTES, ob = sDO + st * C::QT_BYTES;
+            const uint32_t col_s = (gi & 1) ? C::COL_S1 : C::COL_S;
+            if (!(ok = mbar_wait(p_full, gi & 1, abort_flag, p.status, 24))) break;
+            if (it == 0 && k > 0 && !(ok = mbar_wait(acc_empty, (k - 1) & 1, abort_flag, p.status, 37)))
+              break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BQ / 16; ++kk)
+              umma_f16_ts(tmem + C::COL_DV, tmem + col_s + packed_col<BQ, C::NP>(kk), mnmaj<D>(ob, BQ, kk),
+                          ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);  // A = P^T from TMEM
+            if (!(ok = mbar_wait(ds_full, gi & 1, abort_flag, p.status, 26))) break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BQ / 16; ++kk)
+              umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + packed_col<BQ, C::NP>(kk), mnmaj<D>(qb, BQ, kk),
+                          ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);
+            umma_commit(&q_empty[st]);  // dV_i and dK_i were the last readers of dO_i, Q_i
+            if (it + 1 < w.n_all) issue_s_dp(gi + 1, false);
+            if (it + 2 < w.n_all) {
+              if (!(ok = wait_q(gi + 2))) break;
+              tc_fence_after();
+              issue_s_dp(gi + 2, true);
+            }
+            if (gi > 0 && !(ok = mbar_wait(dq_empty, (gi - 1) & 1, abort_flag, p.status, 27))) break;
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              if (C::DQT)
+                umma_f16_ss(tmem + C::COL_DQ, mnmaj<D>(sK, BN, kk), pt_mnmaj(sDS, kk), ID_DQ,
+                            kk > 0 ? 1u : 0u);
+              else
+                umma_f16_ss(tmem + C::COL_DQ, pt_mnmaj(sDS, kk), mnmaj<D>(sK, BN, kk), ID_DQ,
+                            kk > 0 ? 1u : 0u);
+            }
+            umma_commit(dq_full);
+            umma_commit(ds_free);
+          }
+          if (!ok) break;
+          umma_commit(acc_done);
+          umma_commit(kv_empty);
+          g0 += w.n_all;
+        }
+      }
+      for (int k = 0; ok && !C::SDB; ++k) {
         ItemRec e;
         if (!(ok = take_item(k, e, true)) || e.L < 0) break;
         const Walk w = walk(e);
@@ -427,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk)
-            umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + packed_col<BQ>(kk), mnmaj<D>(ob, BQ, kk),
+            umma_f16_ts(tmem + C::COL_DV, tmem + C::COL_S + packed_col<BQ, C::NP>(kk), mnmaj<D>(ob, BQ, kk),
                         ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);  // A = P^T from TMEM
           umma_commit(p_free);
           // S^T for the next query tile overlaps the softmax warps' dS work.
@@ -446,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BQ / 16; ++kk)
-            umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + packed_col<BQ>(kk), mnmaj<D>(qb, BQ, kk),
+            umma_f16_ts(tmem + C::COL_DK, tmem + C::COL_DP + packed_col<BQ, C::NP>(kk), mnmaj<D>(qb, BQ, kk),
                         ID_ACC, (it > 0 || kk > 0) ? 1u : 0u);
           if (more) issue_s_dp(gi + 1, false);
           if (gi > 0 && !(ok = mbar_wait(dq_empty, (gi - 1) & 1, abort_flag, p.status, 27))) break;
@@ -470,17 +572,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         g0 += w.n_all;
       }
     }
-  } else if (warp == 10 || warp == 11) {
-    regs_dec<kRegsOther>();  // idle: only completes warpgroup 2's register release
-  } else if (warp < 8) {
+  } else if (warp == W_TMA + 2 || warp == W_TMA + 3) {
+    // idle: only completes the warpgroup's register release
+    if constexpr (C::NP == 2) regs_dec<kRegsOther>();
+  } else if (warp < W_TMA) {
     // ------------------------------------------------------------ P^T / dS^T
-    regs_inc<kRegsSoftmax>();
-    constexpr int QH = BQ / 2;                // query columns per warp half
-    const int hf = warp >> 2;                 // which half of the tile's queries
+    if constexpr (C::NP == 2) regs_inc<kRegsSoftmax>();
+    constexpr int QH = C::QH;                 // query columns per thread
+    const int hf = warp >> 2;                 // which part of the tile's queries
     const int kr = (warp & 3) * 32 + (threadIdx.x & 31);  // key row == TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     const float sl2 = p.scale_log2;
-    const int t256 = threadIdx.x;             // 0..255 over both warpgroups
+    const int t256 = threadIdx.x;             // 0..SWT-1 over the P/dS warpgroups
     bool ok = true;
     int g0 = 0;  // query-tile iterations of earlier items (barrier phases)
     for (int k = 0; ok; ++k) {
@@ -501,25 +604,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       float pre = fetch(0);
       for (int it = 0; it < w.n_all; ++it) {
+#ifdef SCREE_TRACE
+        long long t_mark = clock64();
+#endif
         const int gi = g0 + it;
         const int q0 = q_tile(w, it) * BQ;
-        const int qh0 = q0 + hf * QH;           // first query of this half
+        const int qh0 = q0 + hf * QH;           // first query of this part
         float* lse_s = lds + (gi & 1) * 2 * BQ + hf * QH;
         float* del_s = lds + (gi & 1) * 2 * BQ + BQ + hf * QH;
         if (t256 < 2 * BQ) lds[(gi & 1) * 2 * BQ + t256] = pre;
         if (it + 1 < w.n_all) pre = fetch(it + 1);
-        softmax_group_sync();
+        softmax_group_sync<C::SWT>();
+        SW_MARK(40);
         const bool need_mask = (q0 + BQ > L) || (k0 + BN > L) || (CAUSAL && q0 < k0 + BN - 1);
         // ---- P^T (this half's QH queries) from S^T
-        ok = mbar_wait(s_full, gi & 1, abort_flag, p.status, 28);
+        const uint32_t col_s = (C::SDB && (gi & 1)) ? C::COL_S1 : C::COL_S;
+        ok = C::SDB ? mbar_wait(&s_full[gi & 1], (gi >> 1) & 1, abort_flag, p.status, 28)
+                    : mbar_wait(s_full, gi & 1, abort_flag, p.status, 28);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+        SW_MARK(41);
         tc_fence_after();
         float pr[QH];
-#pragma unroll
-        for (int c = 0; c < QH / 32; ++c)
-          tmem_ld32(lane_base + C::COL_S + hf * QH + c * 32,
-                    *reinterpret_cast<float(*)[32]>(&pr[c * 32]));
+        tmem_ld_cols<QH>(lane_base + col_s + hf * QH, pr);
         tmem_wait_ld();
+        tmem_regs_ready<QH>(pr);
+        SW_MARK(42);
         uint32_t pk[QH / 2];
 #pragma unroll
         for (int c4 = 0; c4 < QH / 4; ++c4) {
@@ -539,41 +648,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           pk[c4 * 2] = Pk2b<T>::pack(pr[c4 * 4], pr[c4 * 4 + 1]);
           pk[c4 * 2 + 1] = Pk2b<T>::pack(pr[c4 * 4 + 2], pr[c4 * 4 + 3]);
         }
-        if (gi > 0) {  // dV_{i-1} read P^T_{i-1} from these columns
+        SW_MARK(43);
+        if (!C::SDB && gi > 0) {  // dV_{i-1} read P^T_{i-1} from these columns
           ok = mbar_wait(p_free, (gi - 1) & 1, abort_flag, p.status, 29);
           if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
         }
+        SW_MARK(44);
         // P^T (16-bit, two per column) over the first QH/2 of the QH fp32 columns
         // this half read: never over the other half's columns (warps w and w+4
         // share TMEM lanes and do not wait for each other).
-        tmem_st_packed<QH / 2>(lane_base + C::COL_S + hf * QH, pk);
+        tmem_st_packed<QH / 2>(lane_base + col_s + hf * QH, pk);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(p_full);
+        SW_MARK(45);
         // ---- dS^T = P^T * (dP^T - Delta)
         ok = mbar_wait(dp_full, gi & 1, abort_flag, p.status, 30);
         if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
+        SW_MARK(46);
         tc_fence_after();
+        constexpr int DPC = QH < 32 ? QH : 32;  // dP^T columns per load
 #pragma unroll
-        for (int c = 0; c < QH / 32; ++c) {
-          float dp[32];
-          tmem_ld32(lane_base + C::COL_DP + hf * QH + c * 32, dp);
+        for (int c = 0; c < QH / DPC; ++c) {
+          float dp[DPC];
+          tmem_ld_cols<DPC>(lane_base + C::COL_DP + hf * QH + c * DPC, dp);
           tmem_wait_ld();
+          tmem_regs_ready<DPC>(dp);
 #pragma unroll
-          for (int e4 = 0; e4 < 8; ++e4) {
-            const float4 d4 = reinterpret_cast<const float4*>(del_s)[c * 8 + e4];
-            pr[c * 32 + e4 * 4 + 0] *= (dp[e4 * 4 + 0] - d4.x);
-            pr[c * 32 + e4 * 4 + 1] *= (dp[e4 * 4 + 1] - d4.y);
-            pr[c * 32 + e4 * 4 + 2] *= (dp[e4 * 4 + 2] - d4.z);
-            pr[c * 32 + e4 * 4 + 3] *= (dp[e4 * 4 + 3] - d4.w);
+          for (int e4 = 0; e4 < DPC / 4; ++e4) {
+            const float4 d4 = reinterpret_cast<const float4*>(del_s)[c * (DPC / 4) + e4];
+            pr[c * DPC + e4 * 4 + 0] *= (dp[e4 * 4 + 0] - d4.x);
+            pr[c * DPC + e4 * 4 + 1] *= (dp[e4 * 4 + 1] - d4.y);
+            pr[c * DPC + e4 * 4 + 2] *= (dp[e4 * 4 + 2] - d4.z);
+            pr[c * DPC + e4 * 4 + 3] *= (dp[e4 * 4 + 3] - d4.w);
           }
         }
 #pragma unroll
         for (int c = 0; c < QH / 2; ++c) pk[c] = Pk2b<T>::pack(pr[2 * c], pr[2 * c + 1]);
+        SW_MARK(47);
         if (gi > 0) {
           ok = mbar_wait(ds_free, (gi - 1) & 1, abort_flag, p.status, 31);
           if (!__all_sync(0xffffffff, ok)) { ok = false; break; }
         }
+        SW_MARK(48);
         // dS^T: into TMEM over dP^T's first columns (A operand of dK) and into
         // smem (B operand of the dQ GEMM).
         tmem_st_packed<QH / 2>(lane_base + C::COL_DP + hf * QH, pk);
@@ -582,8 +699,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(ds_full);
+        SW_MARK(49);
       }
-      // ---- dK, dV epilogue: 32-column chunk c belongs to half c % 2
+      // ---- dK, dV epilogue: 32-column chunk c belongs to part c % NP
       if (ok) {
         ok = mbar_wait(acc_done, k & 1, abort_flag, p.status, 32);
         ok = __all_sync(0xffffffff, ok);
@@ -603,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           T* dst = pass == 0 ? dvrow : dkrow;
 #pragma unroll
           for (int c = 0; c < D / 32; ++c) {
-            if ((c & 1) != hf) continue;
+            if ((c % C::NP) != hf) continue;
             float v[32];
             tmem_ld32(lane_base + col + c * 32, v);
             tmem_wait_ld();
@@ -627,10 +745,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       g0 += w.n_all;
     }
   } else {
-    // ------------------------------------------------------------ dQ reduction warps 12-15
-    regs_dec<kRegsDq>();
-    const int ln = threadIdx.x - 384;  // TMEM lane: feature d (DQT) or query row
-    const uint32_t lane_base = tmem + ((uint32_t)((warp - 12) * 32) << 16);
+    // ------------------------------------------------------------ dQ reduction warps
+    if constexpr (C::NP == 2) regs_dec<kRegsDq>();
+    const int ln = threadIdx.x - W_DQ * 32;  // TMEM lane: feature d (DQT) or query row
+    const uint32_t lane_base = tmem + ((uint32_t)((warp - W_DQ) * 32) << 16);
     const float sc = p.scale;
     int g0 = 0;  // query-tile iterations of earlier items (barrier phases)
     bool ok = true;
@@ -706,7 +824,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (threadIdx.x < 64) atomicAdd(&g_bwd_trace[threadIdx.x], scree_trace_sm[threadIdx.x]);
 #endif
-  if (warp == 9) {
+  if (warp == W_MMA) {
     tc_fence_after();
     tmem_dealloc<C::TMEM_COLS>(tmem);
   }
@@ -775,7 +893,7 @@ int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
     attr_set[dev & 63] = true;
   }
   ProfScope prof(PROF_ATTN_BWD, s);
-  kern<<<(unsigned)grid, kThreads, BwdCfg<D>::SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
+  kern<<<(unsigned)grid, BwdCfg<D>::THREADS, BwdCfg<D>::SMEM, s>>>(tq, tk, tv, tdo, tdq, p);
   SCREE_LAUNCH_CHECK();
   return SCREE_OK;
 }

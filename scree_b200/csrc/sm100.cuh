@@ -210,6 +210,27 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]), "=f"(v[4]), "=f"(v[5]), "=f"(v[6]),
+        "=f"(v[7]), "=f"(v[8]), "=f"(v[9]), "=f"(v[10]), "=f"(v[11]), "=f"(v[12]), "=f"(v[13]),
+        "=f"(v[14]), "=f"(v[15])
+      : "r"(taddr));
+}
+// N columns (16 or a multiple of 32) into v[0, N); no wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, float* v) {
+  if constexpr (N == 16) {
+    tmem_ld16(taddr, v);
+  } else {
+#pragma unroll
+    for (int c = 0; c < N / 32; ++c)
+      tmem_ld32(taddr + c * 32, *reinterpret_cast<float(*)[32]>(v + c * 32));
+  }
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -276,10 +297,20 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t* v) {
       "r"(v[15])
       : "memory");
 }
-// N (16 or a multiple of 32) packed columns from registers.
+// 32 lanes x 8 consecutive 32-bit columns from registers (raw bits).
+__device__ __forceinline__ void tmem_st8u(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(
+                   taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]),
+               "r"(v[7])
+               : "memory");
+}
+// N (8, 16 or a multiple of 32) packed columns from registers.
 template <int N>
 __device__ __forceinline__ void tmem_st_packed(uint32_t taddr, const uint32_t* v) {
-  if constexpr (N == 16) {
+  if constexpr (N == 8) {
+    tmem_st8u(taddr, v);
+  } else if constexpr (N == 16) {
     tmem_st16u(taddr, v);
   } else {
 #pragma unroll
