@@ -16,11 +16,13 @@
 // whose shared-memory port is its limit: 0.58 of the burst GEMM peak against
 // the separate pass's x re-read of T x C x 2 bytes.)
 //
-// Tiles: 128 rows x BNT (= 256 or 128) columns, K in steps of 64 (128-byte
-// swizzled rows), a 4-stage TMA ring; one persistent CTA per SM walks its tiles
-// with the accumulator double-buffered in TMEM.  Warp 0 issues TMA, warp 1 the
-// MMAs (M = 128, N = BNT), warps 2-5 are the epilogue warps (warp w owns TMEM
-// lanes 32 (w % 4) ..).
+// N a multiple of 256: CTA pairs (clusters of two) with 256 x 256 pair tiles,
+// M = 256 tcgen05 MMAs over both CTAs' shared memory and TMEM, a 6-stage TMA
+// ring of 32 KB per CTA (rmsnorm_qkv_pair_kernel).  Otherwise single CTAs with
+// 128 x 128 tiles and a 4-stage ring (rmsnorm_qkv_kernel).  K in steps of 64
+// (128-byte swizzled rows); persistent CTAs (pairs) walk their tiles with the
+// accumulator double-buffered in TMEM.  Warp 0 issues TMA, warp 1 the MMAs,
+// warps 2-5 are the epilogue warps (warp w owns TMEM lanes 32 (w % 4) ..).
 #include <algorithm>
 #include "attn_common.cuh"
 
@@ -199,6 +201,180 @@ __global__ void __launch_bounds__(kQThreads, 1)
   }
 }
 
+// ------------------------------------------------------------ CTA-pair GEMM
+// Same computation with the tiles of a CTA pair (cluster of two): a pair tile is
+// 256 rows x 256 columns; CTA r of the pair stages rows [128 r, 128 r + 128) of
+// the x tile and columns [128 r, 128 r + 128) of the weight tile, and the even
+// CTA issues M = 256, N = 256 tcgen05 MMAs (.cta_group::2) that read both CTAs'
+// shared memory and leave rows 128 r.. of the accumulator in CTA r's TMEM.  Per
+// K = 16 step each SM then stages and reads 8 KB instead of 12 KB (one CTA's
+// 128 x 256 tile), which is what bounds the single-CTA kernel.
+constexpr int PSTAGES = 6;
+struct PCfg {
+  static constexpr int A_BYTES = 128 * QK * 2;  // this CTA's 128 rows: 16 KB
+  static constexpr int B_BYTES = 128 * QK * 2;  // this CTA's 128 columns: 16 KB
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int OFF_BAR = PSTAGES * STAGE;
+  static constexpr int OFF_END = OFF_BAR + 256;
+  static constexpr int SMEM = OFF_END + 1024;
+};
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kQThreads, 1)
+    rmsnorm_qkv_pair_kernel(const __grid_constant__ CUtensorMap tm_x,
+                            const __grid_constant__ CUtensorMap tm_w, const QParams p) {
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC = make_idesc_f16(256, 256, kBF16, false, true);
+  // Persistent pairs: pair c takes pair tiles c, c + gridDim.x / 2, ...
+  const uint32_t rank = cluster_ctarank();
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int nk = (int)(p.C / QK);
+  const int n_tiles_n = (int)(p.N / 256);
+  const int64_t n_tiles = ((p.T + 255) / 256) * n_tiles_n;
+  // (No early exit on the status word: both CTAs of a pair must reach the
+  // cluster barriers; the bounded waits see it and drain instead.)
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PCfg::OFF_BAR);
+  uint64_t* full = bars;                  // [PSTAGES], used in the even CTA: both CTAs' loads
+  uint64_t* empty = full + PSTAGES;       // [PSTAGES], both CTAs: the MMA commit
+  uint64_t* acc_full = empty + PSTAGES;   // [2], both CTAs: the MMA commit after a tile
+  uint64_t* acc_empty = acc_full + 2;     // [2], even CTA: 256 epilogue threads of the pair
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PSTAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 256);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc_pair<512>(tmem_slot);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA (both CTAs)
+    if (elect_one()) {
+      int64_t g = 0;
+      bool ok = true;
+      for (int64_t tile = pair; ok && tile < n_tiles; tile += npairs) {
+        const int m0 = (int)(tile / n_tiles_n) * 256 + (int)rank * 128;
+        const int n0 = (int)(tile % n_tiles_n) * 256 + (int)rank * 128;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int s = (int)(g % PSTAGES);
+          if (g >= PSTAGES &&
+              !(ok = mbar_wait(&empty[s], (uint32_t)(((g / PSTAGES) - 1) & 1), abort_flag, p.status, 75)))
+            break;
+          uint8_t* st = smem + s * PCfg::STAGE;
+          // The even CTA's barrier counts both CTAs' bytes of the stage.
+          if (rank == 0) mbar_expect_tx(&full[s], 2 * PCfg::STAGE);
+          const uint32_t fb = smem_peer(smem_u32(&full[s]), 0);
+          tma_load_2d_pair(st, &tm_x, fb, kt * QK, m0);
+#pragma unroll
+          for (int j = 0; j < 2; ++j)  // 64-column chunks of [QK rows][64 N]
+            tma_load_2d_pair(st + PCfg::A_BYTES + j * QK * 128, &tm_w, fb, n0 + j * 64, kt * QK);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA (even CTA)
+    if (rank == 0 && elect_one()) {
+      bool ok = true;
+      int64_t g = 0;
+      int i = 0;
+      for (int64_t tile = pair; ok && tile < n_tiles; tile += npairs, ++i) {
+        const int b = i & 1;
+        if (i >= 2 && !(ok = mbar_wait(&acc_empty[b], (uint32_t)(((i >> 1) - 1) & 1), abort_flag,
+                                       p.status, 76)))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + b * 256;
+        for (int kt = 0; kt < nk; ++kt, ++g) {
+          const int s = (int)(g % PSTAGES);
+          if (!(ok = mbar_wait(&full[s], (uint32_t)((g / PSTAGES) & 1), abort_flag, p.status, 77)))
+            break;
+          tc_fence_after();
+          const uint32_t a = smem_u32(smem + s * PCfg::STAGE);
+          const uint32_t bb = a + PCfg::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < QK / 16; ++kk)
+            umma_f16_ss_pair(acc, make_sdesc(a + kk * 32, 16, 1024, SW_128B),
+                             make_sdesc(bb + kk * 16 * 128, QK * 128, 1024, SW_128B), IDESC,
+                             (kt > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_pair(smem_u32(&empty[s]));
+          umma_commit_pair(smem_peer(smem_u32(&empty[s]), 1));
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&acc_full[b]));
+        umma_commit_pair(smem_peer(smem_u32(&acc_full[b]), 1));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // row within this CTA's half == TMEM lane
+    const uint32_t ae0 = smem_peer(smem_u32(&acc_empty[0]), 0);
+    const uint32_t ae1 = smem_peer(smem_u32(&acc_empty[1]), 0);
+    int i = 0;
+    for (int64_t tile = pair; tile < n_tiles; tile += npairs, ++i) {
+      const int b = i & 1;
+      bool ok = mbar_wait(&acc_full[b], (uint32_t)((i >> 1) & 1), abort_flag, p.status, 78);
+      if (!__all_sync(0xffffffff, ok)) break;
+      tc_fence_after();
+      const int m0 = (int)(tile / n_tiles_n) * 256 + (int)rank * 128;
+      const int n0 = (int)(tile % n_tiles_n) * 256;
+      const int64_t t = (int64_t)m0 + r;
+      const bool row_ok = t < p.T;
+      const float rs = row_ok ? p.rstd[t] : 0.f;
+      T* yrow = reinterpret_cast<T*>(p.y) + t * p.N + n0;
+      const uint32_t lane_base = tmem + b * 256 + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < 256 / 32; ++c) {
+        float v[32];
+        tmem_ld32_sync(lane_base + c * 32, v);
+        if (c == 256 / 32 - 1) {  // the whole accumulator half is in registers
+          tc_fence_before();
+          mbar_arrive_cluster(b ? ae1 : ae0);
+        }
+        if (row_ok) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float o[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = v[u * 8 + e] * rs;
+            alignas(16) T pk[8];
+            cvt_from_f<T, 8>(o, pk);
+            *reinterpret_cast<uint4*>(yrow + c * 32 + u * 8) = *reinterpret_cast<const uint4*>(pk);
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // no MMA, commit or remote arrival is left for either CTA
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair<512>(tmem);
+  }
+}
+
 // rstd[t] = 1 / sqrt(mean(x[t]^2) + eps): one warp per row, 16-byte loads.
 template <typename T>
 __global__ void __launch_bounds__(256) row_rstd_kernel(const T* __restrict__ x, int64_t rs_x,
@@ -283,6 +459,36 @@ int launch_qkv(const CUtensorMap& tx, const CUtensorMap& tw, const QParams& p, c
   return SCREE_OK;
 }
 
+template <typename T>
+int launch_qkv_pair(const CUtensorMap& tx, const CUtensorMap& tw, const QParams& p, cudaStream_t s) {
+  auto kern = rmsnorm_qkv_pair_kernel<T>;
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (max_pairs[dev & 63] == 0) {
+    SCREE_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PCfg::SMEM));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3((unsigned)(2 * num_sms()), 1, 1);
+    cfg.blockDim = dim3(kQThreads, 1, 1);
+    cfg.dynamicSmemBytes = PCfg::SMEM;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    SCREE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    max_pairs[dev & 63] = std::max(n, 1);
+  }
+  const int64_t tiles = ((p.T + 255) / 256) * (p.N / 256);
+  const unsigned grid = 2u * (unsigned)std::min<int64_t>(tiles, (int64_t)max_pairs[dev & 63]);
+  kern<<<grid, kQThreads, PCfg::SMEM, s>>>(tx, tw, p);
+  SCREE_LAUNCH_CHECK();
+  return SCREE_OK;
+}
+
 }  // namespace
 }  // namespace scree
 
@@ -350,6 +556,10 @@ extern "C" int scree_rmsnorm_qkv_fwd(const void* x, int64_t x_row_stride, const 
   SCREE_LAUNCH_CHECK();
   QParams p{T, N, C, eps, y, rs, device_status_ptr()};
   ProfScope prof(PROF_NORM_FWD, s);
+#ifndef SCREE_QKV_NO_PAIR
+  if (bnt == 256)  // CTA pairs (x boxes of 128 rows per CTA, weight boxes of 64 columns)
+    return bf16 ? launch_qkv_pair<__nv_bfloat16>(tx, tw, p, s) : launch_qkv_pair<__half>(tx, tw, p, s);
+#endif
   if (bf16)
     return bnt == 256 ? launch_qkv<__nv_bfloat16, 256>(tx, tw, p, s)
                       : launch_qkv<__nv_bfloat16, 128>(tx, tw, p, s);

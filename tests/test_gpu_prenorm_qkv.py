@@ -31,7 +31,7 @@ def _check(got, want):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("T,C,N", [(300, 256, 768), (128, 64, 384), (1, 512, 256), (1000, 1024, 3072)])
+@pytest.mark.parametrize("T,C,N", [(300, 256, 768), (128, 64, 384), (1, 512, 256), (1000, 1024, 3072), (4100, 512, 3072)])
 @pytest.mark.parametrize("with_gamma", [True, False])
 def test_rmsnorm_qkv_forward(cuda, dtype, T, C, N, with_gamma):
     from scree_b200.kernels.native import rmsnorm_qkv
