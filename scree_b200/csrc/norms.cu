@@ -319,26 +319,34 @@ __global__ void __launch_bounds__(2 * kBlock) norm_fwd_stream_kernel(
     if (LAYER) {
       // Shifted-data variance with K = the row's first element (see norm_fwd_kernel).
       const float K = Cvt<T>::to_f(src[0].v[0]);
-      float a1[VW], a2[VW];  // one accumulator per vector element: short chains
+      const uint64_t K2 = f2_pack(K, K);
+      // One accumulator per vector element (short chains), element pairs in
+      // packed f32x2 arithmetic.
+      uint64_t a1[VW / 2], a2[VW / 2];
 #pragma unroll
-      for (int e = 0; e < VW; ++e) a1[e] = a2[e] = 0.f;
+      for (int e = 0; e < VW / 2; ++e) a1[e] = a2[e] = 0ull;
 #pragma unroll 4
       for (int v = lane; v < nv; v += 32) {
         float xv[VW];
         const Pack<T, VW> pk = src[v];  // one 16-byte shared load
         unpack_vec<T, VW>(pk, xv);
 #pragma unroll
-        for (int e = 0; e < VW; ++e) {
-          const float d = xv[e] - K;
-          a1[e] += d;
-          a2[e] = fmaf(d, d, a2[e]);
+        for (int e = 0; e < VW / 2; ++e) {
+          const uint64_t d = f2_sub(f2_pack(xv[2 * e], xv[2 * e + 1]), K2);
+          a1[e] = f2_add(a1[e], d);
+          a2[e] = f2_fma(d, d, a2[e]);
         }
       }
       float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-      for (int e = 0; e < VW; ++e) {
-        s1 += a1[e];
-        s2 += a2[e];
+      for (int e = 0; e < VW / 2; ++e) {
+        float p0, p1, q0, q1;
+        f2_unpack(a1[e], p0, p1);
+        f2_unpack(a2[e], q0, q1);
+        s1 += p0;
+        s1 += p1;
+        s2 += q0;
+        s2 += q1;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -349,25 +357,34 @@ __global__ void __launch_bounds__(2 * kBlock) norm_fwd_stream_kernel(
       mu = K + d1;
       rs = 1.0f / sqrtf(fmaxf(s2 * invC - d1 * d1, 0.f) + eps);
     } else {
-      float a2[VW];
+      uint64_t a2[VW / 2];
 #pragma unroll
-      for (int e = 0; e < VW; ++e) a2[e] = 0.f;
+      for (int e = 0; e < VW / 2; ++e) a2[e] = 0ull;
 #pragma unroll 4
       for (int v = lane; v < nv; v += 32) {
         float xv[VW];
         const Pack<T, VW> pk = src[v];  // one 16-byte shared load
         unpack_vec<T, VW>(pk, xv);
 #pragma unroll
-        for (int e = 0; e < VW; ++e) a2[e] = fmaf(xv[e], xv[e], a2[e]);
+        for (int e = 0; e < VW / 2; ++e) {
+          const uint64_t x2 = f2_pack(xv[2 * e], xv[2 * e + 1]);
+          a2[e] = f2_fma(x2, x2, a2[e]);
+        }
       }
       float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < VW; ++e) ss += a2[e];
+      for (int e = 0; e < VW / 2; ++e) {
+        float q0, q1;
+        f2_unpack(a2[e], q0, q1);
+        ss += q0;
+        ss += q1;
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       rs = 1.0f / sqrtf(ss * invC + eps);
     }
     T* dst = y + r * ys;
+    const uint64_t mu2 = f2_pack(mu, mu), rs2 = f2_pack(rs, rs);
 #pragma unroll 4
     for (int v = lane; v < nv; v += 32) {
       float xv[VW], out[VW], wv[VW], bv[VW];
@@ -376,9 +393,12 @@ __global__ void __launch_bounds__(2 * kBlock) norm_fwd_stream_kernel(
       load_params<VW>(params, nv, v, wv);
       if (LAYER) load_params<VW>(params + C, nv, v, bv);
 #pragma unroll
-      for (int e = 0; e < VW; ++e) {
-        const float t = (xv[e] - mu) * rs * wv[e];
-        out[e] = LAYER ? t + bv[e] : t;
+      for (int e = 0; e < VW / 2; ++e) {  // ((x - mu) * rs) * w (+ b), per lane as in scalar code
+        uint64_t x2 = f2_pack(xv[2 * e], xv[2 * e + 1]);
+        if (LAYER) x2 = f2_sub(x2, mu2);
+        uint64_t t = f2_mul(f2_mul(x2, rs2), f2_pack(wv[2 * e], wv[2 * e + 1]));
+        if (LAYER) t = f2_add(t, f2_pack(bv[2 * e], bv[2 * e + 1]));
+        f2_unpack(t, out[2 * e], out[2 * e + 1]);
       }
       store_vec<T, VW>(dst + (int64_t)v * VW, out);
     }
@@ -558,11 +578,14 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
     }
 
   const float invC = 1.0f / (float)C;
-  float accw[VPT][VW], accb[VPT][VW];
+  // Element pairs in packed f32x2 arithmetic (one instruction per pair, each
+  // lane rounded exactly as the scalar operation would be).
+  static_assert(VW % 2 == 0, "pairs of elements");
+  uint64_t accw[VPT][VW / 2], accb[VPT][VW / 2];
 #pragma unroll
   for (int i = 0; i < VPT; ++i)
 #pragma unroll
-    for (int e = 0; e < VW; ++e) accw[i][e] = accb[i][e] = 0.f;
+    for (int e = 0; e < VW / 2; ++e) accw[i][e] = accb[i][e] = 0ull;
 
   // The row statistics of block j + 1 are loaded while block j is processed,
   // so their latency is not exposed when the ring slot is already full.
@@ -599,7 +622,8 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
       const Pack<T, VW>* xr = reinterpret_cast<const Pack<T, VW>*>(sl + (size_t)k * row_bytes);
       const Pack<T, VW>* dr = reinterpret_cast<const Pack<T, VW>*>(sl + (size_t)(R + k) * row_bytes);
       const bool live = r0 + k < rows;
-      float s0 = 0.f, s1 = 0.f;
+      const uint64_t mu2 = f2_pack(mu[k], mu[k]), rs2 = f2_pack(rs[k], rs[k]);
+      uint64_t s0 = 0ull, s1 = 0ull;
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int v = threadIdx.x + i * NT;
@@ -610,18 +634,23 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
           unpack_vec<T, VW>(pd, dd);
           load_params<VW>(params, nv, v, wp);
 #pragma unroll
-          for (int e = 0; e < VW; ++e) {
-            const float xh = (xx[e] - mu[k]) * rs[k];
-            const float gv = dd[e] * wp[e];
-            accw[i][e] = fmaf(dd[e], xh, accw[i][e]);
-            if (LAYER) accb[i][e] += dd[e];
-            s0 += gv;
-            s1 = fmaf(gv, xh, s1);
+          for (int e = 0; e < VW / 2; ++e) {
+            const uint64_t x2 = f2_pack(xx[2 * e], xx[2 * e + 1]);
+            const uint64_t d2 = f2_pack(dd[2 * e], dd[2 * e + 1]);
+            const uint64_t xh = f2_mul(f2_sub(x2, mu2), rs2);
+            const uint64_t gv = f2_mul(d2, f2_pack(wp[2 * e], wp[2 * e + 1]));
+            accw[i][e] = f2_fma(d2, xh, accw[i][e]);
+            if (LAYER) accb[i][e] = f2_add(accb[i][e], d2);
+            s0 = f2_add(s0, gv);
+            s1 = f2_fma(gv, xh, s1);
           }
         }
       }
-      sums[2 * k] = s0;
-      sums[2 * k + 1] = s1;
+      float a0, a1, b0, b1;
+      f2_unpack(s0, a0, a1);
+      f2_unpack(s1, b0, b1);
+      sums[2 * k] = a0 + a1;
+      sums[2 * k + 1] = b0 + b1;
     }
     constexpr int Q2 = 2 * R, LPQ = 32 / Q2;  // lanes per row sum
     const int buf = (int)(j & 1);
@@ -656,6 +685,8 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
       const Pack<T, VW>* dr = reinterpret_cast<const Pack<T, VW>*>(sl + (size_t)(R + k) * row_bytes);
       const float mg = LAYER ? sums[2 * k] * invC : 0.f;
       const float mgx = sums[2 * k + 1] * invC;
+      const uint64_t mu2 = f2_pack(mu[k], mu[k]), rs2 = f2_pack(rs[k], rs[k]);
+      const uint64_t mg2 = f2_pack(mg, mg), nmgx2 = f2_pack(-mgx, -mgx);
 #pragma unroll
       for (int i = 0; i < VPT; ++i) {
         const int v = threadIdx.x + i * NT;
@@ -666,9 +697,12 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
           unpack_vec<T, VW>(pd, dd);
           load_params<VW>(params, nv, v, wp);
 #pragma unroll
-          for (int e = 0; e < VW; ++e) {
-            const float xh = (xx[e] - mu[k]) * rs[k];
-            out[e] = rs[k] * (dd[e] * wp[e] - mg - xh * mgx);
+          for (int e = 0; e < VW / 2; ++e) {
+            const uint64_t xh =
+                f2_mul(f2_sub(f2_pack(xx[2 * e], xx[2 * e + 1]), mu2), rs2);
+            const uint64_t g =
+                f2_sub(f2_mul(f2_pack(dd[2 * e], dd[2 * e + 1]), f2_pack(wp[2 * e], wp[2 * e + 1])), mg2);
+            f2_unpack(f2_mul(rs2, f2_fma(xh, nmgx2, g)), out[2 * e], out[2 * e + 1]);
           }
           store_vec<T, VW>(dx + (r0 + k) * (int64_t)C + (int64_t)v * VW, out);
         }
@@ -690,9 +724,16 @@ __global__ void __launch_bounds__(NT, 1) norm_bwd_stream_kernel(
       const int v = threadIdx.x + i * NT;
       if (v < nv)
 #pragma unroll
-        for (int e = 0; e < VW; ++e) {
-          part_w[prow * C + (int64_t)v * VW + e] = accw[i][e];
-          if (LAYER && part_b) part_b[prow * C + (int64_t)v * VW + e] = accb[i][e];
+        for (int e = 0; e < VW / 2; ++e) {
+          float w0, w1, b0, b1;
+          f2_unpack(accw[i][e], w0, w1);
+          f2_unpack(accb[i][e], b0, b1);
+          part_w[prow * C + (int64_t)v * VW + 2 * e] = w0;
+          part_w[prow * C + (int64_t)v * VW + 2 * e + 1] = w1;
+          if (LAYER && part_b) {
+            part_b[prow * C + (int64_t)v * VW + 2 * e] = b0;
+            part_b[prow * C + (int64_t)v * VW + 2 * e + 1] = b1;
+          }
         }
     }
   }
