@@ -437,7 +437,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["native", "reference"], default="native")
     ap.add_argument("--config", default="cfg4", choices=["cfg4", "cfg2", "cfg5"])
-    ap.add_argument("--e2e-steps", type=int, default=6)
+    ap.add_argument("--e2e-steps", type=int, default=16,
+                    help="pipelined end-to-end steps timed (the first copy-in and last copy-out are not overlapped)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-norms", action="store_true", help="skip the cfg3 norms/softmax/gathers object")
