@@ -186,10 +186,11 @@ def _cpu_threads():
     return cores
 
 
-def _cpu_head_step(lengths, H, D, causal, head, seed=0):
-    """One step of the CPU sample: the numpy oracle's fwd+bwd (fp32) on head
-    `head` of every sequence of the workload.  Inputs are drawn per head from a
-    seeded generator (N(0,1), as on the GPU)."""
+def _cpu_head_step(lengths, H, D, causal, head, seed=0, fwd_only=False):
+    """One step of the CPU sample: the numpy oracle's fwd+bwd (fp32; the
+    forward alone with `fwd_only`) on head `head` of every sequence of the
+    workload.  Inputs are drawn per head from a seeded generator (N(0,1), as on
+    the GPU)."""
     import oracle
 
     rng = np.random.default_rng(seed + head)
@@ -198,19 +199,20 @@ def _cpu_head_step(lengths, H, D, causal, head, seed=0):
     q, k, v, do = (rng.standard_normal((T, 1, D), dtype=np.float32) for _ in range(4))
     t0 = time.perf_counter()
     oracle.attention_fwd(q, k, v, offs, causal=causal, dtype=np.float32)
-    oracle.attention_bwd(do, q, k, v, offs, causal=causal, dtype=np.float32)
+    if not fwd_only:
+        oracle.attention_bwd(do, q, k, v, offs, causal=causal, dtype=np.float32)
     return time.perf_counter() - t0
 
 
-def cpu_reference_rate(lengths, H, D, causal, repeats=2):
+def cpu_reference_rate(lengths, H, D, causal, repeats=2, fwd_only=False):
     """CPU baseline for the GPU line: the oracle on one head of every sequence,
     `repeats` times (about 10-20 s); tokens/s = T / (H x median head time)."""
     cores = _cpu_threads()
-    times = [_cpu_head_step(lengths, H, D, causal, head=h) for h in range(repeats)]
+    times = [_cpu_head_step(lengths, H, D, causal, head=h, fwd_only=fwd_only) for h in range(repeats)]
     t = statistics.median(times)
     T = sum(lengths)
     rate = T / (t * H)
-    sample = (f"numpy oracle (restatement of scree.kernels.reference) fp32 fwd+bwd of 1 of {H} heads "
+    sample = (f"numpy oracle (restatement of scree.kernels.reference) fp32 {'forward' if fwd_only else 'fwd+bwd'} of 1 of {H} heads "
               f"over all {len(lengths)} sequences (T={T}, D={D}), median of {len(times)} heads = {t:.2f} s; "
               f"x{H} heads (independent, identical cost) for the whole workload")
     return rate, cores, sample
@@ -222,13 +224,14 @@ def run_reference_arm(args, lengths, H, D, causal):
     if rank != 0:
         return
     cores = _cpu_threads()
+    fo = getattr(args, "fwd_only", False)
     for i in range(args.warmup):
-        _cpu_head_step(lengths, H, D, causal, head=i % H)
-    times = [_cpu_head_step(lengths, H, D, causal, head=i % H) for i in range(args.steps)]
+        _cpu_head_step(lengths, H, D, causal, head=i % H, fwd_only=fo)
+    times = [_cpu_head_step(lengths, H, D, causal, head=i % H, fwd_only=fo) for i in range(args.steps)]
     dt = sum(times) / len(times)
     T_total = sum(lengths)
     value = T_total / (dt * H)
-    sample = (f"each step: numpy oracle (restatement of scree.kernels.reference) fp32 fwd+bwd of one of "
+    sample = (f"each step: numpy oracle (restatement of scree.kernels.reference) fp32 {'forward' if fo else 'fwd+bwd'} of one of "
               f"the {H} heads (rotating) over all {len(lengths)} sequences (T={T_total}, D={D}) on {cores} "
               f"host threads, {dt:.2f} s per head; value = T / ({H} x that time): heads are independent "
               f"and cost the same")
@@ -248,17 +251,17 @@ def run_reference_arm(args, lengths, H, D, causal):
         "dtype": "f32",
         "data": "synthetic",
         "config": workload_config(args, lengths, H, D, causal, world),
-        "tflops": workloads_flops(lengths, 1, D, causal) / dt / 1e12,
+        "tflops": workloads_flops(lengths, 1, D, causal, fwd_only=fo) / dt / 1e12,
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def workloads_flops(lengths, H, D, causal):
+def workloads_flops(lengths, H, D, causal, fwd_only=False):
     from scree_b200 import workloads
 
-    return workloads.attn_flops(lengths, H, D, causal)
+    return workloads.attn_flops(lengths, H, D, causal, fwd=True, bwd=not fwd_only)
 
 
 _LEN_DESC = {
@@ -271,7 +274,8 @@ _LEN_DESC = {
 def workload_config(args, lengths, H, D, causal, world):
     return {
         "workload": f"{args.config}: {len(lengths)} seqs {_LEN_DESC[args.config]} seed 0, "
-        f"T={sum(lengths)}, H={H}, D={D}, {getattr(args, 'dtype_name', 'bfloat16')}, {'causal' if causal else 'non-causal'} fwd+bwd",
+        f"T={sum(lengths)}, H={H}, D={D}, {getattr(args, 'dtype_name', 'bfloat16')}, {'causal' if causal else 'non-causal'} "
+        f"{'forward only' if getattr(args, 'fwd_only', False) else 'fwd+bwd'}",
         "global_batch": int(sum(lengths)),
         "seqs": len(lengths),
         "max_seqlen": int(max(lengths)),
@@ -444,6 +448,8 @@ def main():
     ap.add_argument("--no-norms", action="store_true", help="skip the cfg3 norms/softmax/gathers object")
     ap.add_argument("--no-gather", action="store_true", help="N>1: skip the with-output-exchange timing")
     ap.add_argument("--non-causal", action="store_true")
+    ap.add_argument("--fwd-only", action="store_true",
+                    help="time the forward alone (inference; cfg5 is specified forward only)")
     ap.add_argument("--shard", choices=["seqs", "heads"], default="seqs",
                     help="multi-GPU split: whole sequences (default) or sequences split by head groups")
     ap.add_argument("--suite", choices=["attention", "norms"], default="attention",
@@ -522,8 +528,13 @@ def main():
         calls.append((qg, kg, vg, dog, cug))
     q, k, v, do, cu = calls[0]  # whole-sequence mode: the only group
 
+    from scree_b200.kernels.native import varlen_attention_triton
+
     def step():
         for qg, kg, vg, dog, cug in calls:
+            if args.fwd_only:
+                varlen_attention_triton(qg.detach(), kg.detach(), vg.detach(), cug, causal=causal)
+                continue
             for t in (qg, kg, vg):
                 t.grad = None
             out = varlen_attention_triton_autograd(qg, kg, vg, cug, causal=causal)
@@ -581,11 +592,14 @@ def main():
         def step_gather():
             # Step i's outputs travel while step i+1 computes; its requests are
             # waited on after step i+1 is enqueued.
-            for t in (q, k, v):
-                t.grad = None
-            out = varlen_attention_triton_autograd(q, k, v, cu, causal=causal)
-            out.backward(do)
-            sent = [out.detach(), q.grad, k.grad, v.grad]
+            if args.fwd_only:
+                sent = [varlen_attention_triton(q.detach(), k.detach(), v.detach(), cu, causal=causal)]
+            else:
+                for t in (q, k, v):
+                    t.grad = None
+                out = varlen_attention_triton_autograd(q, k, v, cu, causal=causal)
+                out.backward(do)
+                sent = [out.detach(), q.grad, k.grad, v.grad]
             _, reqs = gplan.run(sent, defer=True)
             for r in (pending.pop()[0] if pending else []):
                 r.wait()
@@ -615,18 +629,18 @@ def main():
         g_ms = g0.elapsed_time(g1)
         gm = torch.tensor([g_ms / g_steps], dtype=torch.float64, device=dev)
         dist.all_reduce(gm, op=dist.ReduceOp.MAX)
-        recv_bytes = 4 * (T_all - mine.tokens) * H * D * q.element_size()
+        recv_bytes = (1 if args.fwd_only else 4) * (T_all - mine.tokens) * H * D * q.element_size()
         with_gather = {
             "ms_per_step": float(gm[0]),
             "steps": g_steps,
             "value": float(sum(lengths)) / (float(gm[0]) / 1e3),
             "unit": "tokens/s",
-            "collective": "NCCL send/recv to rank 0 of every rank's O, dQ, dK, dV rows, one message per sequence and tensor straight into rank 0's global-order outputs, one batch per step (NVLink), overlapping the next step's compute",
+            "collective": (f"NCCL send/recv to rank 0 of every rank's {'O' if args.fwd_only else 'O, dQ, dK, dV'} rows, one message per sequence and tensor straight into rank 0's global-order outputs, one batch per step (NVLink), overlapping the next step's compute"),
             "timing": "one CUDA-event pair over all steps on the compute stream, max over ranks, last transfer included",
             "bytes_into_rank0_per_step": int(recv_bytes),
         }
 
-    flops_mine = sum(workloads.attn_flops(ls, hs, D, causal) for hs, ls in groups)
+    flops_mine = sum(workloads.attn_flops(ls, hs, D, causal, fwd=True, bwd=not args.fwd_only) for hs, ls in groups)
     flops_fwd_mine = sum(workloads.attn_flops(ls, hs, D, causal, fwd=True, bwd=False) for hs, ls in groups)
     flops_bwd_mine = sum(workloads.attn_flops(ls, hs, D, causal, fwd=False, bwd=True) for hs, ls in groups)
     stats = torch.tensor([elapsed_ms, float(T), flops_mine, float(launches)], dtype=torch.float64, device=dev)
@@ -658,13 +672,19 @@ def main():
     fwd_avg_ms = fwd_ms / max(nf, 1)
     # This rank's FLOPs per step over its kernel time per step (one launch per
     # step and kind, or one per head-count group with --shard heads).
-    ach_bwd = flops_bwd_mine / (bwd_ms / args.steps / 1e3) / 1e12
-    ach_fwd = flops_fwd_mine / (fwd_ms / args.steps / 1e3) / 1e12
-    traffic, traffic_src = scaled_traffic(groups, D, causal)
+    ach_bwd = flops_bwd_mine / (bwd_ms / args.steps / 1e3) / 1e12 if bwd_ms > 0 else 0.0
+    ach_fwd = flops_fwd_mine / (fwd_ms / args.steps / 1e3) / 1e12 if fwd_ms > 0 else 0.0
+    ach_top = ach_fwd if args.fwd_only else ach_bwd  # the dominant kernel of the step
+    if args.fwd_only:
+        traffic, traffic_src = None, "no DRAM capture of the forward kernel at this size"
+    else:
+        traffic, traffic_src = scaled_traffic(groups, D, causal)
 
     # ------------------------------------------------------------ end to end
     e2e = None
     if not args.no_e2e:
+        n_in = 3 if args.fwd_only else 4  # q, k, v (, dO) in; out (, dq, dk, dv) back
+        n_out = 1 if args.fwd_only else 4
         hq, hk, hv, hdo = (t.detach().cpu().pin_memory() for t in (q, k, v, do))
         ho = torch.empty_like(hq).pin_memory()
         hdq, hdk, hdv = (torch.empty_like(hq).pin_memory() for _ in range(3))
@@ -684,20 +704,25 @@ def main():
             with torch.cuda.stream(cin):
                 if free_ev[i % 2] is not None:
                     cin.wait_event(free_ev[i % 2])
-                for b, hsrc in zip(sset, (hq, hk, hv, hdo)):
+                for b, hsrc in list(zip(sset, (hq, hk, hv, hdo)))[:n_in]:
                     b.copy_(hsrc, non_blocking=True)
                 ready = torch.cuda.Event()
                 ready.record(cin)
             comp.wait_event(ready)
-            qi, ki, vi = (b.detach().requires_grad_(True) for b in sset[:3])
-            out = varlen_attention_triton_autograd(qi, ki, vi, cu, causal=causal)
-            out.backward(sset[3])
+            if args.fwd_only:
+                out = varlen_attention_triton(sset[0], sset[1], sset[2], cu, causal=causal)
+                results = (out,)
+            else:
+                qi, ki, vi = (b.detach().requires_grad_(True) for b in sset[:3])
+                out = varlen_attention_triton_autograd(qi, ki, vi, cu, causal=causal)
+                out.backward(sset[3])
+                results = (out.detach(), qi.grad, ki.grad, vi.grad)
             done = torch.cuda.Event()
             done.record(comp)
             free_ev[i % 2] = done
             with torch.cuda.stream(cout):
                 cout.wait_event(done)
-                for hdst, t in zip((ho, hdq, hdk, hdv), (out.detach(), qi.grad, ki.grad, vi.grad)):
+                for hdst, t in zip((ho, hdq, hdk, hdv), results):
                     hdst.copy_(t, non_blocking=True)
                     t.record_stream(cout)
 
@@ -724,14 +749,17 @@ def main():
             "value": total_T / (e_step / 1e3),
             "unit": "tokens/s",
             "ms_per_step": e_step,
-            "h2d_bytes_per_step": int(4 * nbytes),  # q, k, v, dO
-            "d2h_bytes_per_step": int(4 * nbytes),  # out, dq, dk, dv
-            "path": "varlen_attention_triton_autograd with pinned host q/k/v/dO in, out/dq/dk/dv back to pinned host; copies in, compute and copies out of consecutive steps overlap on three streams",
+            "h2d_bytes_per_step": int(n_in * nbytes),  # q, k, v (, dO)
+            "d2h_bytes_per_step": int(n_out * nbytes),  # out (, dq, dk, dv)
+            "path": ("varlen_attention_triton with pinned host q/k/v in, out back to pinned host"
+                     if args.fwd_only else
+                     "varlen_attention_triton_autograd with pinned host q/k/v/dO in, out/dq/dk/dv back to pinned host")
+            + "; copies in, compute and copies out of consecutive steps overlap on three streams",
         }
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, cores, sample = cpu_reference_rate(lengths, H, D, causal)
+        rate, cores, sample = cpu_reference_rate(lengths, H, D, causal, fwd_only=args.fwd_only)
         cpu = {"value": rate, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
 
     norms = None
@@ -770,20 +798,21 @@ def main():
             "tflops_frac_of_burst_peak": tflops / (peak_burst * world),
             "tflops_frac_of_sustained_peak": tflops / (peak_sus * world),
             "roofline": {
-                "kernel": "attn_bwd_kernel<128, bf16, causal> (dK/dV/dQ, 10*H*D*pairs FLOPs)",
+                "kernel": (f"attn_fwd_kernel<{D}, {'causal' if causal else 'full'}> (4*H*D*pairs FLOPs)" if args.fwd_only
+                           else f"attn_bwd_kernel<{D}, {'causal' if causal else 'full'}> (dK/dV/dQ, 10*H*D*pairs FLOPs)"),
                 "bound": "tensor",
-                "achieved": ach_bwd,
+                "achieved": ach_top,
                 "peak": peak_tf,
                 "unit": "TFLOP/s",
-                "frac": ach_bwd / peak_tf,
-                "frac_of_burst_peak": ach_bwd / peak_burst,
-                "frac_of_sustained_peak": ach_bwd / peak_sus,
+                "frac": ach_top / peak_tf,
+                "frac_of_burst_peak": ach_top / peak_burst,
+                "frac_of_sustained_peak": ach_top / peak_sus,
                 "peak_source": (f"{peak_kind} {peak_name} (MEASURED_PEAKS.json), chosen by the clock record "
                                 f"({'power-capped' if capped else 'unthrottled'})" if peak_kind == "measured"
                                 else "fallback (1.59 PFLOP/s burst, 1.4 sustained)"),
                 "traffic": traffic,
                 "traffic_source": traffic_src,
-                "avg_launch_ms": bwd_avg_ms,
+                "avg_launch_ms": fwd_avg_ms if args.fwd_only else bwd_avg_ms,
             },
             "kernels": {
                 "attn_fwd": {"avg_ms": fwd_avg_ms, "launches": nf, "tflops": ach_fwd, "frac": ach_fwd / peak_tf},
