@@ -452,8 +452,9 @@ def main():
                     help="time the forward alone (inference; cfg5 is specified forward only)")
     ap.add_argument("--shard", choices=["seqs", "heads"], default="seqs",
                     help="multi-GPU split: whole sequences (default) or sequences split by head groups")
-    ap.add_argument("--suite", choices=["attention", "norms"], default="attention",
-                    help="norms: cfg3 RMSNorm/LayerNorm fwd+bwd and pack/unpack/to_padded/from_padded")
+    ap.add_argument("--suite", choices=["attention", "norms", "qkv"], default="attention",
+                    help="norms: cfg3 RMSNorm/LayerNorm fwd+bwd and pack/unpack/to_padded/from_padded; "
+                         "qkv: the fused RMSNorm -> QKV projection alone")
     ap.add_argument("--max-seqs", type=int, default=0, help="keep only the first N sequences (small profiling case)")
     args = ap.parse_args()
 
@@ -461,6 +462,13 @@ def main():
 
     if args.suite == "norms":
         run_norm_suite(args)
+        return
+    if args.suite == "qkv":
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps({"suite": "qkv", "steps": args.steps, "warmup": max(3, args.warmup),
+                          "prenorm_qkv": measure_prenorm_qkv(args.steps, args.warmup)}), flush=True)
         return
     cfg = workloads.attn_config(args.config)
     lengths = list(cfg.lengths)
